@@ -1,0 +1,485 @@
+"""DIA SpMV / SpMSpM benchmark on B200 (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline (the JSON line's `value`): FP32 DIA SpMV y = A*x on config 5 (3D
+27-point stencil, 256x256x1024, n = 67,108,864, 27 diagonals), A
+row-partitioned over N GPUs with a +-65,793-column x halo exchanged over
+NCCL (strong scaling: the matrix is fixed, each GPU gets n/N rows).
+`value` = algorithmic bytes 4*(nnz + 2n) of the whole matrix / max-over-ranks
+step time, in GB/s.  `secondary` holds C = A*A on the same matrix (useful
+GFLOP/s and byte roofline) and, at N = 1, configs 1-4.
+
+Inputs are generated on the device by the library's counter-based generator
+(seeded, uniform [-1, 1]); every timed input is larger than the 126 MB L2
+except config 1, which is timed per launch with an L2 flush in between.
+
+--impl reference times the reference's own CPU SpMV (spmv_from_recon,
+spmv/test/test_tc_spmv.cu:64-79, compiled from the reference sources into
+oracle/_ref/) on the host cores, on a bounded row sample of config 5.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N5 = 256 * 256 * 1024
+OFF5 = np.array([i + 256 * j + 65536 * k for k in (-1, 0, 1) for j in (-1, 0, 1)
+                 for i in (-1, 0, 1)], np.int32)
+SEED_A, SEED_X = 5001, 5002
+REF_SAMPLE_ROWS = 4 * 1024 * 1024
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def spmv_bytes(n, offsets, r0, r1):
+    nnz = sum(max(0, min(r1, n - int(d)) - max(r0, -int(d))) for d in offsets)
+    return 4 * (nnz + 2 * (r1 - r0)), nnz
+
+
+# ------------------------------------------------------------------ clocks
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, gpus):
+        self.gpus = gpus
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms",
+                 "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not self.path:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9 or not f[0].isdigit() or int(f[0]) not in self.gpus:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------- timing
+
+def timed(fn, steps, warmup, *, flush=None, per_launch=False):
+    """Mean ms of fn() over `steps` after `warmup`, CUDA events on the
+    current stream; with per_launch each call is bracketed by its own events
+    and preceded by flush() (outside the bracket)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    if per_launch:
+        tot = 0.0
+        for _ in range(steps):
+            if flush is not None:
+                flush()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            e.synchronize()
+            tot += s.elapsed_time(e)
+        return tot / steps
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        fn()
+    e.record()
+    e.synchronize()
+    return s.elapsed_time(e) / steps
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+# ------------------------------------------------------------ workloads
+
+def spmspm_useful(n, A_off, B_off, sym, r0, r1):
+    """Exact useful flops 2 * sum over pairs of the rows in [r0, r1) where
+    A[i, i+da], B[i+da, i+dc] and C[i, i+dc] all exist."""
+    tot = 0
+    for c, dc in enumerate(sym["C_off"]):
+        for q in range(sym["pair_ptr"][c], sym["pair_ptr"][c + 1]):
+            da = int(A_off[sym["pair_a"][q]])
+            lo = max(r0, 0, -da, -int(dc))
+            hi = min(r1, n, n - da, n - int(dc))
+            tot += max(0, hi - lo)
+    return 2 * tot
+
+
+def nnz_rows(n, offs, r0, r1):
+    return sum(max(0, min(r1, n - int(d)) - max(r0, -int(d))) for d in offs)
+
+
+def l2_flusher():
+    buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")  # 256 MB > L2
+
+    def flush():
+        buf.zero_()
+    return flush
+
+
+def roofline(achieved_gbs, hbm, src, traffic=None):
+    return {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": hbm, "unit": "GB/s",
+            "frac": round(achieved_gbs / hbm, 4), "peak_source": src, "traffic": traffic}
+
+
+def secondary_spmspm(dg, name, n, A, B, steps, warmup, hbm, src, flush=None):
+    sym = dg.spmspm_symbolic(n, A.offsets, B.offsets)
+    Cm = dg.DiaRows.empty(n, n, sym["C_off"], device="cuda", zero=True)
+    fn = lambda: dg.spmspm(A, B, Cm, symbolic=sym)
+    ms = timed(fn, steps, warmup, flush=flush, per_launch=flush is not None)
+    nnzA = nnz_rows(n, A.offsets, 0, n)
+    nnzB = 0 if B is A else nnz_rows(n, B.offsets, 0, n)
+    nnzC = int(sym["C_len"].astype(np.int64).sum())
+    byts = 4 * (nnzA + nnzB + nnzC)
+    fl = spmspm_useful(n, A.offsets, B.offsets, sym, 0, n)
+    del Cm
+    return {"workload": name, "metric": "spmspm_useful_GFLOPs", "value": round(fl / ms / 1e6, 2),
+            "unit": "GFLOP/s", "ms": round(ms, 4), "bytes": byts, "useful_flops": fl,
+            "c_diagonals": len(sym["C_off"]), "pairs": len(sym["pair_a"]),
+            "roofline": roofline(byts / ms / 1e6, hbm, src), "gpu_launches_per_step": 2}
+
+
+def single_gpu_extras(dg, steps, warmup, hbm, src):
+    out = []
+    flush = l2_flusher()
+    # config 1: 2D Poisson SpMV (29 MB: L2-resident, flushed per launch)
+    n = 1 << 20
+    offs = np.array([-1024, -1, 0, 1, 1024], np.int32)
+    A = dg.DiaRows.synth(n, n, offs, seed=101, base=[-1, -1, 4, -1, -1], lo=-0.01, hi=0.01)
+    x = dg.synth_vector(n, seed=102)
+    y = torch.empty(A.stride, device="cuda")
+    ms = timed(lambda: dg.spmv(A, x, y), steps, warmup, flush=flush, per_launch=True)
+    b, nnz = spmv_bytes(n, offs, 0, n)
+    out.append({"workload": "config1 2D 5-pt Poisson n=1048576 SpMV (L2 flushed per launch)",
+                "metric": "spmv_GBps", "value": round(b / ms / 1e6, 1), "unit": "GB/s",
+                "ms": round(ms, 4), "bytes": b, "roofline": roofline(b / ms / 1e6, hbm, src),
+                "gpu_launches_per_step": 1})
+    del A, x, y
+    # config 2: 3D 7-point stencil C = A*A
+    n = 128 ** 3
+    offs = np.array([-16384, -128, -1, 0, 1, 128, 16384], np.int32)
+    A = dg.DiaRows.synth(n, n, offs, seed=201)
+    out.append(secondary_spmspm(dg, "config2 3D 7-pt 128^3 C=A*A", n, A, A, steps, warmup, hbm,
+                                src, flush=flush))
+    del A
+    # config 3: scattered 32 + 32 offsets, normal values
+    n = 1_000_000
+    rng = np.random.default_rng(301)
+
+    def scat():
+        s = {0}
+        while len(s) < 32:
+            s.add(int(rng.integers(-512, 513)))
+        return np.array(sorted(s), np.int32)
+    A = dg.DiaRows.synth(n, n, scat(), seed=303, kind=1, lo=0.0, hi=1.0)
+    B = dg.DiaRows.synth(n, n, scat(), seed=304, kind=1, lo=0.0, hi=1.0)
+    out.append(secondary_spmspm(dg, "config3 scattered 32x32 offsets n=1e6 C=A*B", n, A, B,
+                                steps, warmup, hbm, src))
+    del A, B
+    # config 4: dense band gemm_diag (reference argument set)
+    n, hb = 262144, 64
+    goff = np.arange(-hb, hb + 1, dtype=np.int32)
+    DA = dg.DiaRows.synth(n, n, goff, seed=401).vals[:, :n].contiguous()
+    DB = dg.DiaRows.synth(n, n, goff, seed=402).vals[:, :n].contiguous()
+    co, cl, k2i, kl, tot = dg.gemm_diag_layout(n, goff, goff)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    dco, dcl, dk2i, doff = t(co), t(cl), t(k2i), t(goff)
+    C = torch.zeros(tot, device="cuda")
+    fn = lambda: dg.gemm_diag(DA, DB, doff, doff, n, C, dco, dcl, dk2i, beta=0, h_off_A=goff,
+                              h_off_B=goff)
+    ms = timed(fn, max(3, steps // 4), warmup)
+    byts = 4 * (2 * nnz_rows(n, goff, 0, n) + tot)
+    sym = dg.spmspm_symbolic(n, goff, goff)
+    fl = spmspm_useful(n, goff, goff, sym, 0, n)
+    out.append({"workload": "config4 dense band hb=64 n=262144 gemm_diag (beta=0)",
+                "metric": "gemm_diag_useful_GFLOPs", "value": round(fl / ms / 1e6, 2),
+                "unit": "GFLOP/s", "ms": round(ms, 4), "bytes": byts, "useful_flops": fl,
+                "roofline": roofline(byts / ms / 1e6, hbm, src), "mode": "auto"})
+    return out
+
+
+def cpu_port_baseline(hbm_unused=None):
+    """The oracle's CPU SpMV (C, OpenMP over all host threads) on rows
+    [0, REF_SAMPLE_ROWS) of config 5."""
+    import oracle
+    S = REF_SAMPLE_ROWS
+    rows = oracle.synth_rowidx(SEED_A, N5, N5, OFF5, row0=0, nrows=S)
+    xw = oracle.synth_vector(SEED_X, S + int(OFF5.max()))
+    thr = oracle.threads()
+    oracle.spmv_rowidx(OFF5, rows, rows.shape[1], xw, ncols=N5, nrows=S, nthreads=thr)
+    reps = 5
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        oracle.spmv_rowidx(OFF5, rows, rows.shape[1], xw, ncols=N5, nrows=S, nthreads=thr)
+    sec = (time.perf_counter() - t0) / reps
+    b, _ = spmv_bytes(N5, OFF5, 0, S)
+    return {"value": round(b / sec / 1e9, 2), "unit": "GB/s", "cores": thr, "kind": "port",
+            "sample": f"config 5 rows [0, {S}) ({S * 27 / 1e6:.0f}M entries), mean of {reps}"}
+
+
+# ------------------------------------------------------------------ arms
+
+def setup_dist(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus and world > 1:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def run_ours(args):
+    import diagpu_b200 as dg
+    from diagpu_b200.dist import DistSpmspm, DistSpmv, Halo
+
+    world, rank, local = setup_dist(args)
+    hbm, src = peaks()
+    K, W = args.steps, args.warmup
+    halo = Halo(N5, world, rank, int(OFF5.min()), int(OFF5.max()))
+    r0, r1 = halo.r0, halo.r1
+    A = dg.DiaRows.synth(N5, N5, OFF5, SEED_A, vrow0=r0, nrows=r1 - r0)
+    ds = DistSpmv(A, halo)
+    dg.synth_vector(r1 - r0, SEED_X, i0=r0, out=ds.x_own)
+    launches = []
+    ds.step(launches)
+    per_step = len(launches)
+    torch.cuda.synchronize()
+
+    # headline: K full steps (halo exchange + interior + boundary)
+    for _ in range(W):
+        ds.step()
+    barrier(world)
+    with Clocks(list(range(world))) as clk:
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(K):
+            ds.step()
+        e.record()
+        e.synchronize()
+        barrier(world)
+    ms = max_over_ranks(s.elapsed_time(e) / K, world)
+    total_bytes, nnz = spmv_bytes(N5, OFF5, 0, N5)
+    value = total_bytes / ms / 1e6
+
+    # dominant kernel alone (this rank's whole block, no exchange)
+    rank_bytes, _ = spmv_bytes(N5, OFF5, r0, r1)
+    kms = timed(lambda: dg.spmv(A, ds.x_ext, ds.y, x_lo=halo.xlo), K, W, per_launch=True)
+    kms = max_over_ranks(kms, world)
+
+    # end to end through the public API: pinned host x -> device, SpMV, y -> host
+    xh = torch.empty(r1 - r0, dtype=torch.float32).pin_memory()
+    xh.copy_(ds.x_own.cpu())
+    yh = torch.empty(r1 - r0, dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        ds.x_own.copy_(xh, non_blocking=True)
+        ds.step()
+        yh.copy_(ds.y[:r1 - r0], non_blocking=True)
+    for _ in range(W):
+        e2e_step()
+    barrier(world)
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(K):
+        e2e_step()
+    e2.record()
+    e2.synchronize()
+    ems = max_over_ranks(s2.elapsed_time(e2) / K, world)
+
+    # secondary: C = A*A on the same partitioned matrix
+    del ds
+    B_ext = dg.DiaRows.empty(N5, N5, OFF5, vrow0=halo.xlo, nrows=halo.width, zero=True)
+    B_ext.vals[:, r0 - halo.xlo:r1 - halo.xlo] = A.vals[:, :r1 - r0]
+    dm = DistSpmspm(A, B_ext, halo)
+    ksp = max(3, min(K, 10))
+    mm_ms = max_over_ranks(timed(lambda: dm.step(), ksp, max(1, min(W, 3))), world)
+    sym = dm.sym
+    fl = spmspm_useful(N5, OFF5, OFF5, sym, 0, N5)
+    nnzC = int(sym["C_len"].astype(np.int64).sum())
+    mm_bytes = 4 * (nnz + nnzC)
+    rank_mm_bytes = 4 * (nnz_rows(N5, OFF5, r0, r1) + nnz_rows(N5, sym["C_off"], r0, r1))
+    secondary = [{
+        "workload": "config5 C=A*A (125 output diagonals, 729 pairs)",
+        "metric": "spmspm_useful_GFLOPs", "value": round(fl / mm_ms / 1e6, 2), "unit": "GFLOP/s",
+        "ms": round(mm_ms, 4), "bytes": mm_bytes, "useful_flops": fl,
+        "GBps": round(mm_bytes / mm_ms / 1e6, 1),
+        "roofline": roofline(rank_mm_bytes / mm_ms / 1e6, hbm, src)}]
+    del dm, B_ext, A
+    torch.cuda.empty_cache()
+
+    cpu = None
+    if world == 1:
+        secondary += single_gpu_extras(dg, K, W, hbm, src)
+        if not args.no_cpu_baseline:
+            cpu = cpu_port_baseline()
+
+    if rank == 0:
+        line = {
+            "metric": "spmv_GBps", "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
+            "steps": K, "warmup": W, "ms_per_step": round(ms, 5), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic: counter-hash uniform[-1,1] values, seeded, generated on device",
+            "config": {"workload": "config5 DIA SpMV y=A*x, 3D 27-point stencil 256x256x1024",
+                       "n": N5, "diagonals": 27, "nnz": nnz, "bytes_per_step": total_bytes,
+                       "parallelism": f"row-block x{world}, NCCL x halo +-65793",
+                       "l2": "inputs 7.8 GB > 126 MB L2 (no flush needed)"},
+            "roofline": roofline(rank_bytes / kms / 1e6, hbm, src),
+            "kernel_ms": round(kms, 5),
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(total_bytes / ems / 1e6, 1), "unit": "GB/s",
+                    "ms_per_step": round(ems, 4),
+                    "h2d_bytes_per_step": 4 * N5, "d2h_bytes_per_step": 4 * N5,
+                    "api": "diagpu_b200.dist.DistSpmv.step (dia_spmv_rows), pinned host x/y"},
+            "clocks": clk.summary(),
+            "gpu_launches": per_step * K,
+            "secondary": secondary,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import ctypes as C
+
+    import oracle
+    lib = oracle.ref("spmv")
+    if lib is None:
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "oracle/_ref/libref_spmv.so not built (needs the reference sources)"}))
+        return
+    S = REF_SAMPLE_ROWS
+    dmax = int(OFF5.max())
+    rows = oracle.synth_rowidx(SEED_A, N5, N5, OFF5, row0=0, nrows=S)
+    cols = S + dmax
+    desc = np.sort(OFF5)[::-1].astype(np.int32)
+    rec = np.zeros((len(desc), cols), np.float32)
+    idx = {int(d): k for k, d in enumerate(OFF5)}
+    c = np.arange(cols)
+    for k, d in enumerate(desc):
+        r = c - int(d)
+        ok = (r >= 0) & (r < S)
+        rec[k, ok] = rows[idx[int(d)], r[ok]]
+    x = oracle.synth_vector(SEED_X, cols)
+    y = np.zeros(S, np.float32)
+    thr = oracle.threads()
+    lib.ref_spmv_from_recon_threads.restype = C.c_double
+    lib.ref_spmv_from_recon_threads.argtypes = [C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                                C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                                C.c_int]
+    p = lambda a: a.ctypes.data_as(C.c_void_p)
+    call = lambda reps: lib.ref_spmv_from_recon_threads(S, cols, len(desc), p(desc), p(rec), p(x),
+                                                        p(y), thr, reps)
+    if args.warmup:
+        call(args.warmup)
+    ms = call(args.steps)
+    b, _ = spmv_bytes(N5, OFF5, 0, S)
+    v = round(b / ms / 1e6, 2)
+    print(json.dumps({
+        "impl": "reference", "metric": "spmv_GBps", "value": v, "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: counter-hash uniform[-1,1] values, seeded",
+        "config": {"workload": "config5 DIA SpMV y=A*x, 3D 27-point stencil 256x256x1024",
+                   "n": N5, "diagonals": 27},
+        "cpu_baseline": {"value": v, "unit": "GB/s", "cores": thr, "kind": "reference",
+                         "sample": f"spmv_from_recon (spmv/test/test_tc_spmv.cu:64-79) on rows "
+                                   f"[0, {S}) of config 5, {thr} threads over row slices"},
+        "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+        flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

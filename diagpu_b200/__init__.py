@@ -1,0 +1,296 @@
+"""diagpu_b200 -- B200-native DIA sparse linear algebra (host side).
+
+The compute lives in ``libdiagpu_b200.so`` (CUDA for sm_100a, C ABI declared
+in ``include/diagpu_b200.h``).  This module binds that ABI with ctypes and
+exposes it on torch CUDA tensors; torch is used only for device memory and
+streams.  There is no CPU implementation here: every function raises if the
+library is missing or the tensors are not on a CUDA device.
+
+Entry points mirror the reference's launch surfaces:
+  spmv_recon        launch_tc_spmv_regdirect (spmv/src/dia_reconstruct.cuh:139-144)
+  spmv              CPU CSR loop semantics on the padded rows layout
+                    (spmv/bench/bench_cusparse.cu:119-126)
+  spmspm_symbolic   make_c_structure + pair lists (spmspm/bench_spmspm.cu:109-243)
+  spmspm_hm         gather_meta_kernel argument set (spmspm/spmspm.cu:256-319)
+  spmspm            the same product on the padded rows layout
+  gemm_diag         gemm_diag_kernel argument set (gemm_diag/gemm_diag.cu:119-131)
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libdiagpu_b200.so")
+
+DIA_OK, DIA_ERR_INVALID, DIA_ERR_CUDA, DIA_ERR_UNSUPPORTED, DIA_ERR_CAPACITY = range(5)
+GEMM_AUTO, GEMM_SIMT, GEMM_TCGEN05 = 0, 1, 2
+ALIGN = 32  # floats per stride unit (128 bytes)
+
+_lib = None
+
+
+class DiaError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__(f"[{code}] {msg}")
+        self.code = code
+
+
+def lib():
+    """The loaded CUDA library (raises if it was not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise DiaError(DIA_ERR_UNSUPPORTED,
+                           f"{LIB_PATH} missing: build it with __graft_entry__.build()")
+        L = C.CDLL(LIB_PATH)
+        i, i64, u64, f, p = C.c_int, C.c_int64, C.c_uint64, C.c_float, C.c_void_p
+        L.dia_last_error.restype = C.c_char_p
+        L.dia_version.restype = i
+        L.dia_spmv_recon.argtypes = [i, i, i, p, p, p, i, p, p]
+        L.dia_spmv_rows.argtypes = [i64, i64, i, p, p, i64, i64, i64, i64, p, i64, i64, p, p]
+        L.dia_spmspm_symbolic.argtypes = [i, p, i, p, i, p, p, p, p, p, p, p, p]
+        L.dia_spmspm_hm.argtypes = [p, p, p, p, i, p, p, p, p, p, p, p, p, i, i, p]
+        L.dia_spmspm_rows.argtypes = [i64, p, i64, p, i, p, i64, i64, i64, i64, p, i, p, i64,
+                                      p, i, i64, i64, i64, p]
+        L.dia_gemm_diag.argtypes = [p, p, p, p, i, i, i, p, p, p, p, p]
+        L.dia_gemm_diag_ex.argtypes = [p, p, p, p, p, p, i, i, i, p, p, p, p, i, i, p]
+        L.dia_synth_rows.argtypes = [u64, i64, i64, i, p, p, i, f, f, i64, i64, i64, p, p]
+        L.dia_synth_vector.argtypes = [u64, i64, i64, f, f, p, p]
+        for name in ("dia_spmv_recon", "dia_spmv_rows", "dia_spmspm_symbolic", "dia_spmspm_hm",
+                     "dia_spmspm_rows", "dia_gemm_diag", "dia_gemm_diag_ex", "dia_synth_rows",
+                     "dia_synth_vector"):
+            getattr(L, name).restype = i
+        _lib = L
+    return _lib
+
+
+def check(rc):
+    if rc != DIA_OK:
+        raise DiaError(rc, lib().dia_last_error().decode())
+
+
+def _stream(stream=None):
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+def _dptr(t, dtype=None):
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise DiaError(DIA_ERR_INVALID, "tensor must be on a CUDA device")
+    if dtype is not None and t.dtype != dtype:
+        raise DiaError(DIA_ERR_INVALID, f"expected {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise DiaError(DIA_ERR_INVALID, "tensor must be contiguous")
+    return C.c_void_p(t.data_ptr())
+
+
+def round_stride(rows: int) -> int:
+    return (rows + ALIGN - 1) // ALIGN * ALIGN
+
+
+# ------------------------------------------------------------------ storage
+
+@dataclass
+class DiaRows:
+    """A row block of an n_rows x n_cols DIA matrix in the padded rows layout.
+
+    vals[k, i - vrow0] = A[i, i + offsets[k]] for global rows
+    i in [vrow0, vrow0 + nrows); zero where the column leaves [0, n_cols) and
+    in the stride padding.  A whole matrix is the block with vrow0 = 0,
+    nrows = n_rows.
+    """
+    n_rows: int
+    n_cols: int
+    offsets: np.ndarray      # host int32 [K]
+    d_offsets: torch.Tensor  # device int32 [K]
+    vals: torch.Tensor       # device float32 [K, stride]
+    vrow0: int = 0
+    nrows: int | None = None
+
+    def __post_init__(self):
+        if self.nrows is None:
+            self.nrows = self.n_rows - self.vrow0
+
+    @property
+    def K(self):
+        return len(self.offsets)
+
+    @property
+    def stride(self):
+        return self.vals.shape[1]
+
+    @property
+    def nnz(self):
+        """Stored (in-range) entries of this block's rows."""
+        r0, r1 = self.vrow0, self.vrow0 + self.nrows
+        return int(sum(max(0, min(r1, self.n_cols - int(d)) - max(r0, -int(d)))
+                       for d in self.offsets))
+
+    @property
+    def max_abs_offset(self):
+        return int(np.abs(self.offsets).max()) if self.K else 0
+
+    @staticmethod
+    def empty(n_rows, n_cols, offsets, *, vrow0=0, nrows=None, device="cuda", zero=True):
+        offsets = np.ascontiguousarray(offsets, np.int32)
+        nrows = n_rows - vrow0 if nrows is None else nrows
+        alloc = torch.zeros if zero else torch.empty
+        vals = alloc((len(offsets), round_stride(nrows)), dtype=torch.float32, device=device)
+        d_off = torch.from_numpy(offsets.copy()).to(device)
+        return DiaRows(n_rows, n_cols, offsets, d_off, vals, vrow0, nrows)
+
+    @staticmethod
+    def synth(n_rows, n_cols, offsets, seed, *, kind=0, lo=-1.0, hi=1.0, base=None, vrow0=0,
+              nrows=None, device="cuda", stream=None):
+        """Generate a row block with the library's counter-based generator
+        (value depends only on seed, offset and global row)."""
+        A = DiaRows.empty(n_rows, n_cols, offsets, vrow0=vrow0, nrows=nrows, device=device,
+                          zero=False)
+        d_base = None
+        if base is not None:
+            d_base = torch.as_tensor(np.asarray(base, np.float32), device=device)
+        with torch.cuda.device(A.vals.device):
+            check(lib().dia_synth_rows(seed, n_rows, n_cols, A.K, _dptr(A.d_offsets),
+                                       _dptr(d_base), kind, lo, hi, vrow0, A.nrows, A.stride,
+                                       _dptr(A.vals), _stream(stream)))
+        return A
+
+    @staticmethod
+    def from_host(n_rows, n_cols, offsets, vals_rows, *, vrow0=0, device="cuda"):
+        """From a host [K, nrows] array in rows layout (no padding needed)."""
+        vals_rows = np.asarray(vals_rows, np.float32)
+        A = DiaRows.empty(n_rows, n_cols, offsets, vrow0=vrow0, nrows=vals_rows.shape[1],
+                          device=device)
+        A.vals[:, :vals_rows.shape[1]] = torch.from_numpy(vals_rows).to(device)
+        return A
+
+    def to_host_rows(self):
+        return self.vals[:, :self.nrows].cpu().numpy()
+
+
+def synth_vector(n, seed, *, lo=-1.0, hi=1.0, i0=0, device="cuda", out=None, stream=None):
+    out = torch.empty(n, dtype=torch.float32, device=device) if out is None else out
+    with torch.cuda.device(out.device):
+        check(lib().dia_synth_vector(seed, i0, n, lo, hi, _dptr(out), _stream(stream)))
+    return out
+
+
+# --------------------------------------------------------------------- SpMV
+
+def spmv_recon(rows, cols, d_offsets, d_values, x, y=None, x_size=None, stream=None):
+    """y = A*x for the reference's ReconView (column-indexed, K x cols)."""
+    y = torch.empty(rows, dtype=torch.float32, device=x.device) if y is None else y
+    xs = x.numel() if x_size is None else x_size
+    check(lib().dia_spmv_recon(rows, cols, d_offsets.numel(), _dptr(d_offsets, torch.int32),
+                               _dptr(d_values, torch.float32), _dptr(x, torch.float32), xs,
+                               _dptr(y, torch.float32), _stream(stream)))
+    return y
+
+
+def spmv(A: DiaRows, x, y=None, *, x_lo=0, row_lo=None, row_hi=None, stream=None):
+    """y = A*x over the block's rows (or [row_lo, row_hi)).  x holds global
+    columns [x_lo, x_lo + len(x)); y is indexed from the block's first row."""
+    y = torch.empty(A.stride, dtype=torch.float32, device=A.vals.device) if y is None else y
+    lo = A.vrow0 if row_lo is None else row_lo
+    hi = A.vrow0 + A.nrows if row_hi is None else row_hi
+    check(lib().dia_spmv_rows(A.n_rows, A.n_cols, A.K, _dptr(A.d_offsets), _dptr(A.vals),
+                              A.stride, A.vrow0, lo, hi, _dptr(x, torch.float32), x_lo,
+                              x_lo + x.numel(), _dptr(y, torch.float32), _stream(stream)))
+    return y
+
+
+# ------------------------------------------------------------------- SpMSpM
+
+def spmspm_symbolic(n, A_off, B_off):
+    """Output structure and pair lists of C = A*B (host, exact)."""
+    A_off = np.ascontiguousarray(A_off, np.int32)
+    B_off = np.ascontiguousarray(B_off, np.int32)
+    L = lib()
+    nc = C.c_int(0)
+    npairs = C.c_int64(0)
+    pa = lambda a: a.ctypes.data_as(C.c_void_p)
+    check(L.dia_spmspm_symbolic(n, pa(A_off), len(A_off), pa(B_off), len(B_off), C.byref(nc),
+                                None, None, None, C.byref(npairs), None, None, None))
+    C_off = np.empty(nc.value, np.int32)
+    C_len = np.empty(nc.value, np.int32)
+    C_start = np.empty(nc.value, np.int64)
+    ptr = np.empty(nc.value + 1, np.int32)
+    pair_a = np.empty(max(npairs.value, 1), np.int32)
+    pair_b = np.empty(max(npairs.value, 1), np.int32)
+    check(L.dia_spmspm_symbolic(n, pa(A_off), len(A_off), pa(B_off), len(B_off), C.byref(nc),
+                                pa(C_off), pa(C_len), pa(C_start), C.byref(npairs), pa(ptr),
+                                pa(pair_a), pa(pair_b)))
+    return dict(C_off=C_off, C_len=C_len, C_start=C_start, pair_ptr=ptr,
+                pair_a=pair_a[:npairs.value], pair_b=pair_b[:npairs.value])
+
+
+def spmspm_hm(A_values, A_starts, A_off, A_len, B_values, B_starts, B_len, B_lookup, C_values,
+              C_starts, C_off, C_len, n, stream=None):
+    """C = A*B with gather_meta_kernel's arguments (device tensors; starts int64)."""
+    check(lib().dia_spmspm_hm(_dptr(A_values, torch.float32), _dptr(A_starts, torch.int64),
+                              _dptr(A_off, torch.int32), _dptr(A_len, torch.int32),
+                              A_off.numel(), _dptr(B_values, torch.float32),
+                              _dptr(B_starts, torch.int64), _dptr(B_len, torch.int32),
+                              _dptr(B_lookup, torch.int32), _dptr(C_values, torch.float32),
+                              _dptr(C_starts, torch.int64), _dptr(C_off, torch.int32),
+                              _dptr(C_len, torch.int32), C_off.numel(), n, _stream(stream)))
+    return C_values
+
+
+def spmspm(A: DiaRows, B: DiaRows, C_out: DiaRows | None = None, *, b_lo=None, b_hi=None,
+           symbolic=None, stream=None):
+    """C = A*B on the rows layout.  A and C cover the same row block; B may
+    be a wider block (the halo rows of a partitioned product)."""
+    n = A.n_rows
+    if symbolic is None:
+        symbolic = spmspm_symbolic(n, A.offsets, B.offsets)
+    if C_out is None:
+        C_out = DiaRows.empty(n, n, symbolic["C_off"], vrow0=A.vrow0, nrows=A.nrows,
+                              device=A.vals.device, zero=True)
+    b_lo = B.vrow0 if b_lo is None else b_lo
+    b_hi = B.vrow0 + B.nrows if b_hi is None else b_hi
+    check(lib().dia_spmspm_rows(n, _dptr(A.vals), A.stride, _dptr(A.d_offsets), A.K,
+                                _dptr(B.vals), B.stride, B.vrow0, b_lo, b_hi,
+                                _dptr(B.d_offsets), B.K, _dptr(C_out.vals), C_out.stride,
+                                _dptr(C_out.d_offsets), C_out.K, A.vrow0, A.vrow0,
+                                A.vrow0 + A.nrows, _stream(stream)))
+    return C_out
+
+
+# ---------------------------------------------------------------- gemm_diag
+
+def gemm_diag(DA, DB, off_A, off_B, n, C_data, C_offsets, C_lens, k_to_idx, *, beta=1,
+              mode=GEMM_AUTO, h_off_A=None, h_off_B=None, stream=None):
+    """gemm_diag product on the reference's layouts (device tensors).
+    beta=1 accumulates into C_data like the reference; beta=0 overwrites."""
+    hA = None if h_off_A is None else np.ascontiguousarray(h_off_A, np.int32)
+    hB = None if h_off_B is None else np.ascontiguousarray(h_off_B, np.int32)
+    check(lib().dia_gemm_diag_ex(_dptr(DA, torch.float32), _dptr(DB, torch.float32),
+                                 _dptr(off_A, torch.int32), _dptr(off_B, torch.int32),
+                                 None if hA is None else hA.ctypes.data_as(C.c_void_p),
+                                 None if hB is None else hB.ctypes.data_as(C.c_void_p),
+                                 off_A.numel(), off_B.numel(), n, _dptr(C_data, torch.float32),
+                                 _dptr(C_offsets, torch.int32), _dptr(C_lens, torch.int32),
+                                 _dptr(k_to_idx, torch.int32), beta, mode, _stream(stream)))
+    return C_data
+
+
+def gemm_diag_layout(n, off_A, off_B):
+    """C layout of gemm_diag (build_c_layout, gemm_diag/gemm_diag.cu:387-423):
+    int value starts, lengths, k_to_idx[2n-1], ascending k list, total."""
+    sym = spmspm_symbolic(n, off_A, off_B)
+    k_list = sym["C_off"]
+    starts = sym["C_start"]
+    if len(starts) and int(starts[-1]) + int(sym["C_len"][-1]) >= 2 ** 31:
+        raise DiaError(DIA_ERR_UNSUPPORTED, "gemm_diag layout uses int value starts")
+    k2i = np.full(2 * n - 1, -1, np.int32)
+    k2i[k_list + n - 1] = np.arange(len(k_list), dtype=np.int32)
+    total = int(sym["C_len"].astype(np.int64).sum())
+    return starts.astype(np.int32), sym["C_len"], k2i, k_list, total

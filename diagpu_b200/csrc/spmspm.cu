@@ -1,0 +1,307 @@
+/*
+ * spmspm.cu -- diagonal-pair SpMSpM numeric phase for sm_100a.
+ *
+ * C = A*B in diagonal storage: output diagonal dc receives, for every pair
+ * (a, b) with da + db = dc, the shifted elementwise product
+ *     C[i, i+dc] += A[i, i+da] * B[i+da, i+dc].
+ * Two kernels:
+ *   pair_plan_kernel  -- one CTA per output diagonal resolves its pairs on the
+ *                        device (B found by lookup table or by offset), in A
+ *                        storage order, with an order-preserving ballot
+ *                        compaction, and writes the term list (element
+ *                        offsets + valid rows) to stream-ordered scratch.
+ *   pair_sum_kernel   -- persistent CTAs walk (output diagonal, row tile)
+ *                        work items, output diagonal fastest, so the A and B
+ *                        rows of one tile stay in L2 while all output
+ *                        diagonals of that tile are produced.  Each output
+ *                        value is accumulated in a register and stored once:
+ *                        no atomics, no shared-memory accumulation, and the
+ *                        summation order of the reference CPU oracle
+ *                        (spmspm/bench_spmspm.cu:392-403).
+ * The bound is HBM: bytes 4*(nnzA + nnzB + nnzC) for 2*sum(overlap) flops.
+ */
+#include <algorithm>
+
+#include "../../include/diagpu_b200.h"
+#include "dia_core.cuh"
+
+namespace dia {
+
+/* A diagonal storage scheme reduced to "element offset of row 0" plus the
+ * rows where the diagonal holds a stored value. */
+struct LayoutDesc {
+    int kind;                /* 0 rows layout, 1 HM (size_t starts), 2 HM (int starts) */
+    const int* off;          /* device offsets (read for output diagonals) */
+    const size_t* st64;
+    const int* st32;
+    const int* len;
+    long long stride;        /* kind 0 */
+    long long vrow0;         /* kind 0: global row of element 0 */
+    int rlo, rhi;            /* kind 0: rows present in the buffer */
+    int n;                   /* matrix order */
+};
+
+__device__ __forceinline__ void diag_range(const LayoutDesc& L, int k, int d, long long& base,
+                                           int& lo, int& hi)
+{
+    if (L.kind == 0) {
+        base = (long long)k * L.stride - L.vrow0;
+        lo = max(max(0, -d), L.rlo);
+        hi = min(min(L.n, L.n - d), L.rhi);
+    } else {
+        const long long s = L.kind == 1 ? (long long)L.st64[k] : (long long)L.st32[k];
+        const int m = min(d, 0);
+        base = s + m;
+        lo = -m;
+        hi = L.len[k] - m;
+    }
+}
+
+struct PlanArgs {
+    LayoutDesc A, B, C;
+    int nA, nB, nC;
+    const int* B_off;     /* used when B_lookup is null */
+    const int* B_lookup;  /* [2n-1] or null */
+    int row_lo, row_hi;   /* output rows of this call */
+    int stride_terms;     /* term slots per output diagonal (>= pairs) */
+    Term* terms;
+    OutDesc* outs;
+};
+
+constexpr int kBoffSmem = 2048;
+
+__global__ void __launch_bounds__(kBlock) pair_plan_kernel(PlanArgs p)
+{
+    __shared__ int s_boff[kBoffSmem];
+    __shared__ int s_warp[kBlock / 32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const bool boff_smem = !p.B_lookup && p.nB <= kBoffSmem;
+    if (boff_smem)
+        for (int b = tid; b < p.nB; b += kBlock) s_boff[b] = p.B_off[b];
+    __syncthreads();
+    const int n = p.A.n;
+
+    for (int c = blockIdx.x; c < p.nC; c += gridDim.x) {
+        const int dc = p.C.off[c];
+        OutDesc od;
+        int olo, ohi;
+        diag_range(p.C, c, dc, od.o, olo, ohi);
+        olo = max(olo, p.row_lo);
+        ohi = min(ohi, p.row_hi);
+        if (p.C.kind == 0) {
+            od.wlo = (int)max((long long)p.row_lo, p.C.vrow0);
+            od.whi = (int)min((long long)p.row_hi, p.C.vrow0 + p.C.stride);
+        } else {
+            od.wlo = olo;
+            od.whi = ohi;
+        }
+        if (ohi < olo) ohi = olo;
+        od.olo = olo;
+        od.ohi = ohi;
+        od.t0 = c * p.stride_terms;
+        int count = 0;
+        for (int a0 = 0; a0 < p.nA; a0 += kBlock) {
+            const int a = a0 + tid;
+            bool valid = false;
+            Term t;
+            if (a < p.nA && olo < ohi) {
+                const int da = p.A.off[a];
+                const long long db = (long long)dc - da;
+                int b = -1;
+                if (p.B_lookup) {
+                    if (db > -n && db < n) b = p.B_lookup[db + n - 1];
+                } else {
+                    for (int bb = 0; bb < p.nB; ++bb) {
+                        const int o = boff_smem ? s_boff[bb] : p.B_off[bb];
+                        if (o == db) b = bb; /* last match, as the reference's map */
+                    }
+                }
+                if (b >= 0) {
+                    long long ua, ub;
+                    int alo, ahi, blo, bhi;
+                    diag_range(p.A, a, da, ua, alo, ahi);
+                    diag_range(p.B, b, (int)db, ub, blo, bhi);
+                    t.u = ua;
+                    t.v = ub + da;
+                    t.lo = max(max(alo, blo - da), olo);
+                    t.hi = min(min(ahi, bhi - da), ohi);
+                    valid = t.lo < t.hi;
+                }
+            }
+            const unsigned m = __ballot_sync(0xffffffffu, valid);
+            if (lane == 0) s_warp[warp] = __popc(m);
+            __syncthreads();
+            int woff = 0, total = 0;
+            for (int w = 0; w < kBlock / 32; ++w) {
+                woff += w < warp ? s_warp[w] : 0;
+                total += s_warp[w];
+            }
+            if (valid) {
+                const int pos = count + woff + __popc(m & ((1u << lane) - 1u));
+                p.terms[od.t0 + pos] = t;
+            }
+            count += total;
+            __syncthreads();
+        }
+        od.t1 = od.t0 + count;
+        if (tid == 0) p.outs[c] = od;
+    }
+}
+
+struct SumArgs {
+    const float* U;
+    const float* V;
+    float* O;
+    const OutDesc* outs;
+    const Term* terms;
+    int nOut;
+    int row_lo;
+    int ntiles;
+};
+
+template <bool ACCUM>
+__global__ void __launch_bounds__(kBlock) pair_sum_kernel(SumArgs s)
+{
+    __shared__ Term s_t[kMaxTerms];
+    const long long items = (long long)s.nOut * s.ntiles;
+    for (long long it = blockIdx.x; it < items; it += gridDim.x) {
+        const int c = (int)(it % s.nOut);
+        const int tile_lo = s.row_lo + (int)(it / s.nOut) * kTile;
+        const OutDesc od = s.outs[c];
+        const int wlo = max(od.wlo, tile_lo), whi = min(od.whi, tile_lo + kTile);
+        if (wlo >= whi) continue;
+        const int r0 = tile_lo + (int)threadIdx.x;
+        float acc[kILP];
+#pragma unroll
+        for (int j = 0; j < kILP; ++j) acc[j] = 0.0f;
+        for (int t0 = od.t0; t0 < od.t1; t0 += kMaxTerms) {
+            const int nt = min(kMaxTerms, od.t1 - t0);
+            __syncthreads();
+            for (int q = threadIdx.x; q < nt; q += kBlock) s_t[q] = s.terms[t0 + q];
+            __syncthreads();
+            accumulate_terms<false>(s.U, s.V, s_t, nt, tile_lo, r0, acc);
+        }
+#pragma unroll
+        for (int j = 0; j < kILP; ++j) {
+            const int i = r0 + j * kBlock;
+            if (i >= wlo && i < whi) {
+                const float v = (i >= od.olo && i < od.ohi) ? acc[j] : 0.0f;
+                float* dst = s.O + od.o + i;
+                if (ACCUM)
+                    *dst = __fadd_rn(*dst, v);
+                else
+                    __stcs(dst, v);
+            }
+        }
+    }
+}
+
+/* Launch the persistent pair-sum kernel over nOut output diagonals and the
+ * rows [row_lo, row_hi). */
+int launch_pair_sum(const float* U, const float* V, float* O, const OutDesc* outs,
+                    const Term* terms, int nOut, int row_lo, int row_hi, bool accumulate,
+                    cudaStream_t stream)
+{
+    if (nOut <= 0 || row_hi <= row_lo) return DIA_OK;
+    SumArgs s{U, V, O, outs, terms, nOut, row_lo, (row_hi - row_lo + kTile - 1) / kTile};
+    const long long items = (long long)nOut * s.ntiles;
+    const void* k = accumulate ? (const void*)pair_sum_kernel<true> : (const void*)pair_sum_kernel<false>;
+    long long grid = persistent_blocks(k, 0);
+    grid = std::min(grid, items);
+    if (accumulate)
+        pair_sum_kernel<true><<<(unsigned)grid, kBlock, 0, stream>>>(s);
+    else
+        pair_sum_kernel<false><<<(unsigned)grid, kBlock, 0, stream>>>(s);
+    DIA_TRY_CUDA(cudaGetLastError());
+    return DIA_OK;
+}
+
+static int run_planned(PlanArgs p, const float* U, const float* V, float* O,
+                       cudaStream_t stream)
+{
+    if (p.nC <= 0 || p.row_hi <= p.row_lo) return DIA_OK;
+    p.stride_terms = std::max(p.nA, 1);
+    const size_t term_bytes = (size_t)p.nC * p.stride_terms * sizeof(Term);
+    const size_t out_bytes = (size_t)p.nC * sizeof(OutDesc);
+    void* ws = nullptr;
+    DIA_TRY_CUDA(cudaMallocAsync(&ws, term_bytes + out_bytes, stream));
+    p.terms = (Term*)ws;
+    p.outs = (OutDesc*)((char*)ws + term_bytes);
+    const int grid = std::min(p.nC, 8 * num_sms());
+    pair_plan_kernel<<<grid, kBlock, 0, stream>>>(p);
+    cudaError_t e = cudaGetLastError();
+    int rc = e == cudaSuccess ? DIA_OK : cuda_fail(e, "pair_plan_kernel launch");
+    if (rc == DIA_OK)
+        rc = launch_pair_sum(U, V, O, p.outs, p.terms, p.nC, p.row_lo, p.row_hi, false, stream);
+    cudaError_t ef = cudaFreeAsync(ws, stream);
+    if (rc == DIA_OK && ef != cudaSuccess) rc = cuda_fail(ef, "cudaFreeAsync");
+    return rc;
+}
+
+}  // namespace dia
+
+using namespace dia;
+
+extern "C" int dia_spmspm_hm(const float* d_A_values, const size_t* d_A_starts, const int* d_A_off,
+                             const int* d_A_len, int A_ndiag, const float* d_B_values,
+                             const size_t* d_B_starts, const int* d_B_len, const int* d_B_lookup,
+                             float* d_C_values, const size_t* d_C_starts, const int* d_C_off,
+                             const int* d_C_len, int C_ndiag, int n, cudaStream_t stream)
+{
+    if (n < 0 || A_ndiag < 0 || C_ndiag < 0)
+        return fail(DIA_ERR_INVALID, "dia_spmspm_hm: negative size");
+    if (n == 0 || C_ndiag == 0) return DIA_OK;
+    if (!d_C_values || !d_C_starts || !d_C_off || !d_C_len ||
+        (A_ndiag > 0 && (!d_A_values || !d_A_starts || !d_A_off || !d_A_len || !d_B_values ||
+                         !d_B_starts || !d_B_len || !d_B_lookup)))
+        return fail(DIA_ERR_INVALID, "dia_spmspm_hm: null pointer");
+    if ((long long)n + kTile >= (1LL << 31))
+        return fail(DIA_ERR_UNSUPPORTED, "dia_spmspm_hm: n beyond int32 range");
+    PlanArgs p{};
+    p.A = LayoutDesc{1, d_A_off, d_A_starts, nullptr, d_A_len, 0, 0, 0, 0, n};
+    p.B = LayoutDesc{1, nullptr, d_B_starts, nullptr, d_B_len, 0, 0, 0, 0, n};
+    p.C = LayoutDesc{1, d_C_off, d_C_starts, nullptr, d_C_len, 0, 0, 0, 0, n};
+    p.nA = A_ndiag;
+    p.nB = 0;
+    p.nC = C_ndiag;
+    p.B_lookup = d_B_lookup;
+    p.row_lo = 0;
+    p.row_hi = n;
+    return run_planned(p, d_A_values, d_B_values, d_C_values, stream);
+}
+
+extern "C" int dia_spmspm_rows(int64_t n, const float* d_A_vals, int64_t A_stride,
+                               const int* d_A_off, int nA, const float* d_B_vals,
+                               int64_t B_stride, int64_t b_vrow0, int64_t b_lo, int64_t b_hi,
+                               const int* d_B_off, int nB, float* d_C_vals, int64_t C_stride,
+                               const int* d_C_off, int nC, int64_t vrow0, int64_t row_lo,
+                               int64_t row_hi, cudaStream_t stream)
+{
+    if (n < 0 || nA < 0 || nB < 0 || nC < 0 || A_stride < 0 || B_stride < 0 || C_stride < 0)
+        return fail(DIA_ERR_INVALID, "dia_spmspm_rows: negative size");
+    if (n + kTile >= (1LL << 31))
+        return fail(DIA_ERR_UNSUPPORTED, "dia_spmspm_rows: n beyond int32 range");
+    row_lo = std::max<int64_t>(row_lo, vrow0);
+    row_hi = std::min<int64_t>(row_hi, vrow0 + C_stride);
+    if (nC == 0 || row_hi <= row_lo) return DIA_OK;
+    if (!d_C_vals || !d_C_off || (nA > 0 && (!d_A_vals || !d_A_off || !d_B_vals || !d_B_off)))
+        return fail(DIA_ERR_INVALID, "dia_spmspm_rows: null pointer");
+    if (b_lo < b_vrow0 || b_hi > b_vrow0 + B_stride)
+        return fail(DIA_ERR_INVALID, "dia_spmspm_rows: B rows outside the B buffer");
+    const int in = (int)n;
+    PlanArgs p{};
+    p.A = LayoutDesc{0, d_A_off, nullptr, nullptr, nullptr, A_stride, vrow0, (int)vrow0,
+                     (int)std::min<int64_t>(vrow0 + A_stride, n), in};
+    p.B = LayoutDesc{0, d_B_off, nullptr, nullptr, nullptr, B_stride, b_vrow0,
+                     (int)std::max<int64_t>(b_lo, 0), (int)std::min<int64_t>(b_hi, n), in};
+    p.C = LayoutDesc{0, d_C_off, nullptr, nullptr, nullptr, C_stride, vrow0, (int)vrow0,
+                     (int)std::min<int64_t>(vrow0 + C_stride, n), in};
+    p.nA = nA;
+    p.nB = nB;
+    p.nC = nC;
+    p.B_off = d_B_off;
+    p.B_lookup = nullptr;
+    p.row_lo = (int)row_lo;
+    p.row_hi = (int)row_hi;
+    return run_planned(p, d_A_vals, d_B_vals, d_C_vals, stream);
+}

@@ -1,0 +1,164 @@
+/*
+ * spmv.cu -- FP32 DIA SpMV for sm_100a.
+ *
+ * HBM-streaming design: each CTA owns a tile of kTile consecutive rows; the
+ * term list (one term per diagonal) is built once per CTA in shared memory;
+ * every warp then streams 32 consecutive values of each diagonal (one
+ * coalesced 128-byte line, read with evict-first loads because values are
+ * used once) and the matching shifted window of x (read through L1/L2, where
+ * the K shifted windows of neighbouring rows overlap).  There is no tensor
+ * core work: y = A*x moves 4*(nnz + 2n) bytes for 2*nnz flops, far below the
+ * B200 ridge point, so HBM bandwidth is the bound.
+ *
+ * Reference behaviour (spmv/src/tc_spmv_regdirect_kernel.cu:62-147): y
+ * overwritten, terms whose column leaves [0, cols) or [0, x_size) dropped.
+ * The reference computed in TF32 on mma.sync; this computes in FP32 with the
+ * CPU reference's summation order (spmv/test/test_tc_spmv.cu:64-79 for the
+ * Recon layout, spmv/bench/bench_cusparse.cu:119-126 for ascending offsets).
+ */
+#include "../../include/dia_reconstruct_compat.h"
+#include "../../include/diagpu_b200.h"
+#include "dia_core.cuh"
+
+namespace dia {
+
+struct SpmvArgs {
+    const float* vals;
+    const float* x;
+    float* y;
+    const int* off;
+    int K;
+    int row_lo, row_hi;   /* rows computed */
+    int clo, chi;         /* columns that carry a term */
+    long long u_row0;     /* element offset of (k = 0, row 0) in vals */
+    long long u_kstride;  /* element stride between diagonals */
+    int u_shift_by_d;     /* 1: value of row i at vals[.. + i + d] (Recon) */
+    long long x_base;     /* x element of column c is x[c - x_base] */
+    long long y_base;     /* y element of row i is y[i - y_base] */
+};
+
+template <bool STREAM>
+__global__ void __launch_bounds__(kBlock) spmv_kernel(SpmvArgs a)
+{
+    __shared__ Term s_t[kMaxTerms];
+    const int tile_lo = a.row_lo + (int)blockIdx.x * kTile;
+    const int r0 = tile_lo + (int)threadIdx.x;
+    float acc[kILP];
+#pragma unroll
+    for (int j = 0; j < kILP; ++j) acc[j] = 0.0f;
+
+    for (int k0 = 0; k0 < a.K; k0 += kMaxTerms) {
+        const int nt = min(kMaxTerms, a.K - k0);
+        if (k0) __syncthreads();
+        for (int q = threadIdx.x; q < nt; q += kBlock) {
+            const int k = k0 + q;
+            const int d = a.off[k];
+            Term t;
+            t.u = a.u_row0 + (long long)k * a.u_kstride + (a.u_shift_by_d ? d : 0);
+            t.v = (long long)d - a.x_base;
+            /* rows i with column i + d in [clo, chi), clipped to the rows
+             * computed so no load ever leaves the caller's buffers */
+            long long lo = (long long)a.clo - d, hi = (long long)a.chi - d;
+            lo = lo < a.row_lo ? a.row_lo : lo;
+            hi = hi > a.row_hi ? a.row_hi : hi;
+            if (hi < lo) hi = lo;
+            t.lo = (int)lo;
+            t.hi = (int)hi;
+            s_t[q] = t;
+        }
+        __syncthreads();
+        accumulate_terms<STREAM>(a.vals, a.x, s_t, nt, tile_lo, r0, acc);
+    }
+#pragma unroll
+    for (int j = 0; j < kILP; ++j) {
+        const int i = r0 + j * kBlock;
+        if (i < a.row_hi) a.y[i - a.y_base] = acc[j];
+    }
+}
+
+static int launch_spmv(const SpmvArgs& a, cudaStream_t stream)
+{
+    const long long rows = (long long)a.row_hi - a.row_lo;
+    if (rows <= 0) return DIA_OK;
+    const long long grid = (rows + kTile - 1) / kTile;
+    spmv_kernel<true><<<(unsigned)grid, kBlock, 0, stream>>>(a);
+    DIA_TRY_CUDA(cudaGetLastError());
+    return DIA_OK;
+}
+
+}  // namespace dia
+
+using namespace dia;
+
+extern "C" int dia_spmv_recon(int rows, int cols, int num_diags, const int* d_diag_offsets,
+                              const float* d_values, const float* d_x, int x_size, float* d_y,
+                              cudaStream_t stream)
+{
+    if (rows < 0 || cols < 0 || num_diags < 0 || x_size < 0)
+        return fail(DIA_ERR_INVALID, "dia_spmv_recon: negative size");
+    if (rows == 0) return DIA_OK;
+    if (!d_y || (num_diags > 0 && (!d_diag_offsets || !d_values || !d_x)))
+        return fail(DIA_ERR_INVALID, "dia_spmv_recon: null pointer");
+    if ((long long)rows + kTile >= (1LL << 31))
+        return fail(DIA_ERR_UNSUPPORTED, "dia_spmv_recon: rows beyond int32 range");
+    SpmvArgs a{};
+    a.vals = d_values;
+    a.x = d_x;
+    a.y = d_y;
+    a.off = d_diag_offsets;
+    a.K = num_diags;
+    a.row_lo = 0;
+    a.row_hi = rows;
+    a.clo = 0;
+    a.chi = cols < x_size ? cols : x_size;
+    a.u_row0 = 0;
+    a.u_kstride = cols;
+    a.u_shift_by_d = 1;
+    a.x_base = 0;
+    a.y_base = 0;
+    return launch_spmv(a, stream);
+}
+
+extern "C" int dia_spmv_rows(int64_t n_rows, int64_t n_cols, int num_diags, const int* d_offsets,
+                             const float* d_vals, int64_t stride, int64_t vrow0, int64_t row_lo,
+                             int64_t row_hi, const float* d_x, int64_t x_lo, int64_t x_hi,
+                             float* d_y, cudaStream_t stream)
+{
+    if (n_rows < 0 || n_cols < 0 || num_diags < 0 || stride < 0)
+        return fail(DIA_ERR_INVALID, "dia_spmv_rows: negative size");
+    if (row_lo < 0) row_lo = 0;
+    if (row_hi > n_rows) row_hi = n_rows;
+    if (row_hi <= row_lo) return DIA_OK;
+    if (row_lo < vrow0 || row_hi > vrow0 + stride)
+        return fail(DIA_ERR_INVALID, "dia_spmv_rows: rows outside the stored block");
+    if (!d_y || (num_diags > 0 && (!d_offsets || !d_vals || !d_x)))
+        return fail(DIA_ERR_INVALID, "dia_spmv_rows: null pointer");
+    if (n_rows + kTile >= (1LL << 31) || n_cols >= (1LL << 31))
+        return fail(DIA_ERR_UNSUPPORTED, "dia_spmv_rows: dimensions beyond int32 range");
+    SpmvArgs a{};
+    a.vals = d_vals;
+    a.x = d_x;
+    a.y = d_y;
+    a.off = d_offsets;
+    a.K = num_diags;
+    a.row_lo = (int)row_lo;
+    a.row_hi = (int)row_hi;
+    a.clo = (int)(x_lo > 0 ? x_lo : 0);
+    a.chi = (int)(x_hi < n_cols ? x_hi : n_cols);
+    if (a.chi < a.clo) a.chi = a.clo;
+    a.u_row0 = -vrow0;
+    a.u_kstride = stride;
+    a.u_shift_by_d = 0;
+    a.x_base = x_lo;
+    a.y_base = vrow0;
+    return launch_spmv(a, stream);
+}
+
+/* C++-linkage drop-in for the reference launcher (same mangled signature as
+ * spmv/src/dia_reconstruct.cuh:139-144). */
+void launch_tc_spmv_regdirect(ReconView R, const float* d_x, int x_size, float* d_y,
+                              cudaStream_t stream)
+{
+    dia_spmv_recon(R.rows, R.cols, R.num_diags, R.diag_offsets, R.values, d_x, x_size, d_y,
+                   stream);
+}

@@ -1,0 +1,197 @@
+"""Row-block partitioning and halo exchange across GPUs.
+
+A matrix of order n is split into contiguous row blocks, one per rank
+(a multiple of 32 rows each, so every block starts 128-byte aligned in the
+padded rows layout).  Row i of y = A*x needs x columns i + d for every
+offset d, so rank r, owning rows [r0, r1), needs x on [r0 + min d, r1 + max d):
+its own columns plus a halo of max|d| columns from each neighbour.  For
+C = A*B the same holds for the rows of B (halo = max|d_A|).  The halo is the
+only communication: NCCL point-to-point sends/receives with ranks r-1 and
+r+1 (batched), issued before the interior rows' kernel so the transfer over
+NVLink overlaps the interior compute; the boundary rows run after the
+receive completes.  The reference has no multi-GPU path; this module is the
+partitioned form of its single-GPU products.
+
+The exchange is written against torch.distributed and works with the nccl
+backend (GPU tensors) and gloo (CPU tensors, used by the CPU tests).
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from . import DiaRows, round_stride, spmspm, spmspm_symbolic, spmv
+
+
+def row_block(n: int, world: int, rank: int, align: int = 32):
+    """[r0, r1) of rank's rows: equal shares rounded to `align` rows."""
+    per = -(-n // world)
+    per = -(-per // align) * align
+    r0 = min(n, rank * per)
+    r1 = min(n, r0 + per)
+    return r0, r1
+
+
+def halo_window(n: int, r0: int, r1: int, lo_off: int, hi_off: int):
+    """Global columns [xlo, xhi) rows [r0, r1) touch for offsets in
+    [lo_off, hi_off] (clipped to the matrix)."""
+    return max(0, r0 + min(lo_off, 0)), min(n, r1 + max(hi_off, 0))
+
+
+class Halo:
+    """Halo geometry of one rank for offsets in [lo_off, hi_off]."""
+
+    def __init__(self, n, world, rank, lo_off, hi_off):
+        self.n, self.world, self.rank = n, world, rank
+        self.lo_off, self.hi_off = min(lo_off, 0), max(hi_off, 0)
+        self.r0, self.r1 = row_block(n, world, rank)
+        self.xlo, self.xhi = halo_window(n, self.r0, self.r1, self.lo_off, self.hi_off)
+        for r in range(world):
+            a, b = row_block(n, world, r)
+            if 0 < b - a < max(-self.lo_off, self.hi_off) and world > 1:
+                raise ValueError(f"halo {max(-self.lo_off, self.hi_off)} exceeds rank {r}'s "
+                                 f"{b - a} rows: use fewer ranks")
+        # what each neighbour needs from me
+        self.left = row_block(n, world, rank - 1) if rank > 0 else None
+        self.right = row_block(n, world, rank + 1) if rank < world - 1 else None
+
+    @property
+    def width(self):
+        return self.xhi - self.xlo
+
+    def interior(self):
+        """Rows whose columns all lie in this rank's own [r0, r1)."""
+        a = self.r0 - self.lo_off if self.rank > 0 else self.r0
+        b = self.r1 - self.hi_off if self.rank < self.world - 1 else self.r1
+        a, b = min(max(a, self.r0), self.r1), max(min(b, self.r1), self.r0)
+        return (a, max(a, b))
+
+    def boundary(self):
+        a, b = self.interior()
+        return [(lo, hi) for lo, hi in ((self.r0, a), (b, self.r1)) if hi > lo]
+
+    def start(self, ext: torch.Tensor, group=None):
+        """Post the halo sends/receives on ext (column j = global xlo + j);
+        returns a handle whose wait() completes the exchange."""
+        e2 = ext.view(1, -1) if ext.dim() == 1 else ext
+        ops, post = [], []
+
+        def cols(a, b):
+            return e2[:, a - self.xlo:b - self.xlo]
+
+        def recv(a, b, peer):
+            v = cols(a, b)
+            buf = v if v.is_contiguous() else torch.empty(v.shape, dtype=v.dtype, device=v.device)
+            ops.append(dist.P2POp(dist.irecv, buf, peer, group))
+            if buf is not v:
+                post.append((v, buf))
+
+        def send(a, b, peer):
+            v = cols(a, b)
+            buf = v if v.is_contiguous() else v.contiguous()
+            ops.append(dist.P2POp(dist.isend, buf, peer, group))
+
+        if self.left is not None:
+            lxlo, lxhi = halo_window(self.n, *self.left, self.lo_off, self.hi_off)
+            if self.xlo < self.r0:
+                recv(self.xlo, self.r0, self.rank - 1)
+            if lxhi > self.r0:
+                send(self.r0, lxhi, self.rank - 1)
+        if self.right is not None:
+            rxlo, rxhi = halo_window(self.n, *self.right, self.lo_off, self.hi_off)
+            if self.xhi > self.r1:
+                recv(self.r1, self.xhi, self.rank + 1)
+            if rxlo < self.r1:
+                send(rxlo, self.r1, self.rank + 1)
+        works = dist.batch_isend_irecv(ops) if ops else []
+        return _Pending(works, post)
+
+
+class _Pending:
+    def __init__(self, works, post):
+        self.works, self.post = works, post
+
+    def wait(self):
+        for w in self.works:
+            w.wait()
+        for v, buf in self.post:
+            v.copy_(buf)
+
+
+# ----------------------------------------------------------------- products
+
+class DistSpmv:
+    """y = A*x with A row-partitioned over the process group.
+
+    Each rank holds its row block of A (padded rows layout) and an extended
+    x buffer over its halo window; `step()` exchanges the halo, runs the
+    interior rows concurrently with the transfer, then the boundary rows."""
+
+    def __init__(self, A: DiaRows, halo: Halo, group=None):
+        self.A, self.halo, self.group = A, halo, group
+        dev = A.vals.device
+        self.x_ext = torch.zeros(halo.width, dtype=torch.float32, device=dev)
+        self.y = torch.zeros(A.stride, dtype=torch.float32, device=dev)
+
+    @property
+    def x_own(self):
+        h = self.halo
+        return self.x_ext[h.r0 - h.xlo:h.r1 - h.xlo]
+
+    def step(self, launches: list | None = None):
+        h = self.halo
+        pend = h.start(self.x_ext, self.group) if h.world > 1 else None
+        a, b = h.interior()
+        if b > a:
+            spmv(self.A, self.x_ext, self.y, x_lo=h.xlo, row_lo=a, row_hi=b)
+            if launches is not None:
+                launches.append("spmv")
+        if pend is not None:
+            pend.wait()
+        for lo, hi in h.boundary():
+            spmv(self.A, self.x_ext, self.y, x_lo=h.xlo, row_lo=lo, row_hi=hi)
+            if launches is not None:
+                launches.append("spmv")
+        return self.y
+
+
+class DistSpmspm:
+    """C = A*B with A, B, C row-partitioned; B's halo rows (within max|d_A|
+    of the block) come from the neighbours."""
+
+    def __init__(self, A: DiaRows, B_ext: DiaRows, halo: Halo, group=None):
+        self.A, self.B, self.halo, self.group = A, B_ext, halo, group
+        self.sym = spmspm_symbolic(A.n_rows, A.offsets, B_ext.offsets)
+        self.C = DiaRows.empty(A.n_rows, A.n_cols, self.sym["C_off"], vrow0=A.vrow0,
+                               nrows=A.nrows, device=A.vals.device, zero=True)
+
+    def step(self, launches: list | None = None):
+        h = self.halo
+        pend = h.start(self.B.vals, self.group) if h.world > 1 else None
+        # interior rows: all B rows they touch are this rank's own
+        a, b = h.interior()
+        if b > a:
+            self._rows(a, b, h.r0, h.r1)
+            if launches is not None:
+                launches += ["pair_plan", "pair_sum"]
+        if pend is not None:
+            pend.wait()
+        for lo, hi in h.boundary():
+            self._rows(lo, hi, h.xlo, h.xhi)
+            if launches is not None:
+                launches += ["pair_plan", "pair_sum"]
+        return self.C
+
+    def _rows(self, lo, hi, b_lo, b_hi):
+        from . import _dptr, _stream, check, lib
+        A, B, Cm = self.A, self.B, self.C
+        check(lib().dia_spmspm_rows(A.n_rows, _dptr(A.vals), A.stride, _dptr(A.d_offsets), A.K,
+                                    _dptr(B.vals), B.stride, B.vrow0, b_lo, b_hi,
+                                    _dptr(B.d_offsets), B.K, _dptr(Cm.vals), Cm.stride,
+                                    _dptr(Cm.d_offsets), Cm.K, A.vrow0, lo, hi, _stream()))
+
+
+def offsets_span(offsets):
+    o = np.asarray(offsets)
+    return int(o.min()), int(o.max())

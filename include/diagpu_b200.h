@@ -1,0 +1,170 @@
+/*
+ * diagpu_b200.h -- C ABI of the B200 (sm_100a) DIA sparse linear-algebra
+ * library (libdiagpu_b200.so).
+ *
+ * Conventions
+ *   - Every entry point returns an int status: DIA_OK (0) or one of the
+ *     DIA_ERR_* codes; dia_last_error() gives the calling thread's message.
+ *     Nothing calls exit() (the reference's CUDA_CHECK did).
+ *   - Pointers named d_* are device memory owned by the caller; h_* are host
+ *     memory.  Kernels are enqueued on the given stream and the call returns
+ *     without synchronising unless its comment says otherwise.
+ *   - Values are fp32; summation follows the reference CPU routine's order
+ *     with separately rounded multiply and add, so results equal the CPU
+ *     oracle bit for bit (dense-band tensor-core mode excepted: TF32).
+ *   - Row-indexed padded layout ("rows layout"): vals[k*stride + (i - vrow0)]
+ *     holds A[i, i + off[k]] for global row i; stride is a multiple of 32
+ *     floats (128 bytes) for aligned vector loads; out-of-range entries and
+ *     the stride padding are zero.  A contiguous row block of a partitioned
+ *     matrix is the same layout with vrow0 = the block's first row.
+ *   - HM layout (the reference's SpMSpM layout): diagonal d stored from
+ *     position min(row, col) = row + min(d, 0), length n - |d|.
+ */
+#ifndef DIAGPU_B200_H
+#define DIAGPU_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    DIA_OK = 0,
+    DIA_ERR_INVALID = 1,     /* bad argument (sizes, null pointers, layout) */
+    DIA_ERR_CUDA = 2,        /* a CUDA runtime call or launch failed */
+    DIA_ERR_UNSUPPORTED = 3, /* valid input outside what this build handles */
+    DIA_ERR_CAPACITY = 4     /* caller buffer too small (two-call pattern) */
+};
+
+/* Message for the last failing call on this host thread ("" if none). */
+const char* dia_last_error(void);
+/* Library version, major*10000 + minor*100 + patch. */
+int dia_version(void);
+
+/* ----------------------------------------------------------------- SpMV */
+
+/* y[r] = sum_k values[k*cols + r + d_k] * x[r + d_k] for r in [0, rows),
+ * terms with r + d_k outside [0, min(cols, x_size)) dropped, k in storage
+ * order; y fully overwritten.  d_diag_offsets/d_values form the reference's
+ * ReconView (column-indexed Recon, offsets sorted descending by build_recon).
+ * Replaces launch_tc_spmv_regdirect (spmv/src/dia_reconstruct.cuh:139-144,
+ * spmv/src/tc_spmv_regdirect_kernel.cu:135-147) and computes in FP32 instead
+ * of TF32. */
+int dia_spmv_recon(int rows, int cols, int num_diags, const int* d_diag_offsets,
+                   const float* d_values, const float* d_x, int x_size,
+                   float* d_y, cudaStream_t stream);
+
+/* SpMV on the rows layout, for global rows [row_lo, row_hi):
+ * y[i - vrow0] = sum_k vals[k*stride + i - vrow0] * x[i + d_k - x_lo],
+ * terms with i + d_k outside [0, n_cols) or outside [x_lo, x_hi) dropped.
+ * x holds global columns [x_lo, x_hi) (a row block's own columns plus its
+ * halo).  Same math as the reference's CPU CSR loop
+ * (spmv/bench/bench_cusparse.cu:119-126) when offsets ascend. */
+int dia_spmv_rows(int64_t n_rows, int64_t n_cols, int num_diags,
+                  const int* d_offsets, const float* d_vals, int64_t stride,
+                  int64_t vrow0, int64_t row_lo, int64_t row_hi,
+                  const float* d_x, int64_t x_lo, int64_t x_hi, float* d_y,
+                  cudaStream_t stream);
+
+/* ----------------------------------------------------- SpMSpM symbolic */
+
+/* Host-side symbolic phase of C = A*B (n x n).  C offsets are the ascending
+ * set {da + db : -n < da + db < n} (make_c_structure,
+ * spmspm/bench_spmspm.cu:109-131; compute_c_hm_structure,
+ * spmspm/paper_hm.cuh:87-117; build_c_layout's k-set,
+ * gemm_diag/gemm_diag.cu:387-423), lengths n - |d|, HM starts the prefix
+ * sums.  Pairs feeding each C diagonal are listed in A storage order (the
+ * order cpu_dia_spgemm, spmspm/bench_spmspm.cu:392-403, sums them).
+ * Two-call pattern: pass NULL outputs to get *n_c and *n_pairs, then call
+ * again with buffers of those sizes (pair_ptr has *n_c + 1 entries).
+ * Repeated offsets in A or B are rejected (DIA_ERR_INVALID). */
+int dia_spmspm_symbolic(int n, const int* h_A_off, int nA, const int* h_B_off,
+                        int nB, int* n_c, int* h_C_off, int* h_C_len,
+                        int64_t* h_C_start, int64_t* n_pairs, int* h_pair_ptr,
+                        int* h_pair_a, int* h_pair_b);
+
+/* ------------------------------------------------------ SpMSpM numeric */
+
+/* C = A*B over HM arrays with the argument set of the reference's
+ * gather_spgemm_kernel / gather_meta_kernel (spmspm/spmspm.cu:196-211,
+ * 257-272): signed offsets, size_t starts, lengths, B_lookup[2n-1] (B index
+ * of offset db at db + n - 1, or -1).  Every C position is overwritten.
+ * Pairs are resolved on the device in A order; no host synchronisation.
+ * Uses stream-ordered scratch (cudaMallocAsync) of C_ndiag * A_ndiag * 24
+ * bytes, released on the same stream. */
+int dia_spmspm_hm(const float* d_A_values, const size_t* d_A_starts,
+                  const int* d_A_off, const int* d_A_len, int A_ndiag,
+                  const float* d_B_values, const size_t* d_B_starts,
+                  const int* d_B_len, const int* d_B_lookup,
+                  float* d_C_values, const size_t* d_C_starts,
+                  const int* d_C_off, const int* d_C_len, int C_ndiag, int n,
+                  cudaStream_t stream);
+
+/* C = A*B on the rows layout (A and C share vrow0 and the output rows
+ * [row_lo, row_hi); B holds global rows [b_lo, b_hi) at B_vals[k*B_stride +
+ * r - b_vrow0], i.e. a row block plus its halo).  C rows in [row_lo, row_hi)
+ * are overwritten, zero outside each diagonal's valid range.  Output offsets
+ * d_C_off come from dia_spmspm_symbolic; pairs are resolved on the device.
+ * Stream-ordered scratch of nC * nA * 24 bytes. */
+int dia_spmspm_rows(int64_t n, const float* d_A_vals, int64_t A_stride,
+                    const int* d_A_off, int nA, const float* d_B_vals,
+                    int64_t B_stride, int64_t b_vrow0, int64_t b_lo,
+                    int64_t b_hi, const int* d_B_off, int nB, float* d_C_vals,
+                    int64_t C_stride, const int* d_C_off, int nC,
+                    int64_t vrow0, int64_t row_lo, int64_t row_hi,
+                    cudaStream_t stream);
+
+/* ----------------------------------------------------------- gemm_diag */
+
+/* C += A*B with gemm_diag_kernel's argument set (gemm_diag/gemm_diag.cu:
+ * 121-131): row-packed DA[ri*n + row] (P x n), DB (Q x n), offsets off_A /
+ * off_B, HM-packed C with int value starts C_offsets, C_lens and
+ * k_to_idx[2n-1] from build_c_layout.  Accumulates into C like the
+ * reference (which expects C zeroed), without atomics and deterministically.
+ * Reads the P + Q offsets back to the host to plan the product (one
+ * synchronisation of `stream` per call). */
+int dia_gemm_diag(const float* d_DA, const float* d_DB, const int* d_off_A,
+                  const int* d_off_B, int P, int Q, int n, float* d_C_data,
+                  const int* d_C_offsets, const int* d_C_lens,
+                  const int* d_k_to_idx, cudaStream_t stream);
+
+enum {
+    DIA_GEMM_AUTO = 0,   /* tensor cores for a contiguous dense band */
+    DIA_GEMM_SIMT = 1,   /* exact fp32 diagonal-pair kernel */
+    DIA_GEMM_TCGEN05 = 2 /* tcgen05 TF32 dense-band kernel */
+};
+
+/* dia_gemm_diag with options: beta 0 overwrites C (no read of C), beta 1
+ * accumulates; mode picks the kernel (DIA_GEMM_*).  h_off_A / h_off_B may
+ * be host copies of the offsets (skips the read-back) or NULL. */
+int dia_gemm_diag_ex(const float* d_DA, const float* d_DB, const int* d_off_A,
+                     const int* d_off_B, const int* h_off_A,
+                     const int* h_off_B, int P, int Q, int n, float* d_C_data,
+                     const int* d_C_offsets, const int* d_C_lens,
+                     const int* d_k_to_idx, int beta, int mode,
+                     cudaStream_t stream);
+
+/* ------------------------------------------------ synthetic test inputs */
+
+/* Fill rows [row0, row0+nrows) of a rows-layout matrix (K diagonals, stride)
+ * with the library's counter-based generator: value(seed, d, i) depends only
+ * on the offset and the global row, so any row block can be generated on its
+ * own.  kind 0: base[k] + lo + (hi-lo)*u, u in [0,1) (24-bit); kind 1:
+ * base[k] + hi * (Irwin-Hall-12 normal approximation).  d_base may be NULL.
+ * Out-of-range entries and padding are zero. */
+int dia_synth_rows(uint64_t seed, int64_t n_rows, int64_t n_cols, int K,
+                   const int* d_offsets, const float* d_base, int kind,
+                   float lo, float hi, int64_t row0, int64_t nrows,
+                   int64_t stride, float* d_vals, cudaStream_t stream);
+
+/* out[j] = lo + (hi-lo)*u(seed, i0 + j) for j in [0, len). */
+int dia_synth_vector(uint64_t seed, int64_t i0, int64_t len, float lo, float hi,
+                     float* d_out, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DIAGPU_B200_H */
