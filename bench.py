@@ -465,6 +465,70 @@ def run_reference(args):
         flush=True)
 
 
+def _only_spmv(dg, n, offs):
+    A = dg.DiaRows.synth(n, n, offs, SEED_A)
+    x = dg.synth_vector(n, SEED_X)
+    y = torch.empty(A.stride, device="cuda")
+    return (lambda: dg.spmv(A, x, y)), spmv_bytes(n, offs, 0, n)[0]
+
+
+def _only_spmspm(dg, n, offsA, offsB=None, kind=0):
+    A = dg.DiaRows.synth(n, n, offsA, SEED_A, kind=kind, lo=-1.0 if kind == 0 else 0.0)
+    B = A if offsB is None else dg.DiaRows.synth(n, n, offsB, SEED_X, kind=kind,
+                                                  lo=-1.0 if kind == 0 else 0.0)
+    sym = dg.spmspm_symbolic(n, A.offsets, B.offsets)
+    Cm = dg.DiaRows.empty(n, n, sym["C_off"], zero=True)
+    byts = 4 * (nnz_rows(n, A.offsets, 0, n) + (0 if B is A else nnz_rows(n, B.offsets, 0, n))
+                + int(sym["C_len"].astype(np.int64).sum()))
+    return (lambda: dg.spmspm(A, B, Cm, symbolic=sym)), byts
+
+
+def _scat(seed):
+    rng = np.random.default_rng(seed)
+    s = {0}
+    while len(s) < 32:
+        s.add(int(rng.integers(-512, 513)))
+    return np.array(sorted(s), np.int32)
+
+
+def _only_gemm4(dg, n=262144, hb=64, mode=0):
+    goff = np.arange(-hb, hb + 1, dtype=np.int32)
+    DA = dg.DiaRows.synth(n, n, goff, seed=401).vals[:, :n].contiguous()
+    DB = dg.DiaRows.synth(n, n, goff, seed=402).vals[:, :n].contiguous()
+    co, cl, k2i, kl, tot = dg.gemm_diag_layout(n, goff, goff)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    dco, dcl, dk2i, doff = t(co), t(cl), t(k2i), t(goff)
+    C = torch.zeros(tot, device="cuda")
+    fn = lambda: dg.gemm_diag(DA, DB, doff, doff, n, C, dco, dcl, dk2i, beta=0, h_off_A=goff,
+                              h_off_B=goff, mode=mode)
+    return fn, 4 * (2 * nnz_rows(n, goff, 0, n) + tot)
+
+
+# name -> builder(dg) returning (callable, algorithmic bytes); the "_s" cases
+# are reduced sizes (<= a few GB on the device) for ncu captures
+ONLY = {
+    "spmv5": lambda dg: _only_spmv(dg, N5, OFF5),
+    "spmv5_s": lambda dg: _only_spmv(dg, 256 * 256 * 64, OFF5),
+    "spmv1": lambda dg: _only_spmv(dg, 1 << 20, np.array([-1024, -1, 0, 1, 1024], np.int32)),
+    "spmspm5": lambda dg: _only_spmspm(dg, N5, OFF5),
+    "spmspm5_s": lambda dg: _only_spmspm(dg, 256 * 256 * 64, OFF5),
+    "spmspm2": lambda dg: _only_spmspm(dg, 128 ** 3, np.array([-16384, -128, -1, 0, 1, 128,
+                                                                16384], np.int32)),
+    "spmspm3": lambda dg: _only_spmspm(dg, 1_000_000, _scat(301), _scat(302), kind=1),
+    "gemm4": lambda dg: _only_gemm4(dg),
+    "gemm4_simt": lambda dg: _only_gemm4(dg, mode=1),
+}
+
+
+def run_only(args):
+    import diagpu_b200 as dg
+    torch.cuda.set_device(0)
+    fn, byts = ONLY[args.only](dg)
+    ms = timed(fn, args.steps, args.warmup)
+    print(json.dumps({"only": args.only, "ms": round(ms, 4), "bytes": byts,
+                      "GBps": round(byts / ms / 1e6, 1)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -472,7 +536,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", choices=sorted(ONLY), default=None,
+                    help="run one workload `steps` times (for profiling) and print its time")
     args = ap.parse_args()
+    if args.only:
+        return run_only(args)
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     if args.impl == "reference":

@@ -25,8 +25,9 @@
 namespace dia {
 
 constexpr int kBlock = 256;          /* threads per CTA */
-constexpr int kILP = 8;              /* rows per thread */
-constexpr int kTile = kBlock * kILP; /* rows per work item */
+constexpr int kILP = 4;              /* rows per thread */
+constexpr int kTile = kBlock * kILP; /* rows per tile */
+constexpr int kBatch = 4;            /* terms whose loads are issued together */
 constexpr int kMaxTerms = 384;       /* terms staged in shared memory at once */
 
 /* One term of an output diagonal: element offsets of U and V at row 0 and
@@ -54,18 +55,50 @@ __device__ __forceinline__ float mul_add_rn(float acc, float a, float b)
 }
 
 /* Accumulate terms [0, nt) held in shared memory into acc for the rows
- * r0 + j*kBlock (j < kILP) of the tile [tile_lo, tile_lo + kTile).  Terms
- * whose range covers the whole tile take the unchecked path; terms that
- * touch it partially take the per-row checked path; others are skipped. */
-template <bool STREAM_U>
+ * r0 + j*kBlock (j < kILP) of the tile [tile_lo, tile_lo + kTile).
+ * Terms are taken kBatch at a time: when every term of a batch covers the
+ * whole tile, all kBatch*kILP*2 loads are issued before the first multiply,
+ * so one memory latency is paid per batch instead of per term; the adds are
+ * still applied term by term in list order.  Terms that cover the tile only
+ * partly take the per-row checked path; others are skipped. */
+template <bool STREAM_U, int ILP = kILP, int BATCH = kBatch>
 __device__ __forceinline__ void accumulate_terms(const float* __restrict__ U,
                                                  const float* __restrict__ V,
                                                  const Term* s_terms, int nt,
                                                  int tile_lo, int r0,
-                                                 float (&acc)[kILP])
+                                                 float (&acc)[ILP])
 {
+    constexpr int kTile = kBlock * ILP;
+    constexpr int kILP = ILP;
+    constexpr int kBatch = BATCH;
     const int tile_hi = tile_lo + kTile;
-    for (int q = 0; q < nt; ++q) {
+    int q = 0;
+    for (; q + kBatch <= nt; q += kBatch) {
+        Term t[kBatch];
+        bool full = true;
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            t[u] = s_terms[q + u];
+            full &= (t[u].lo <= tile_lo) & (tile_hi <= t[u].hi);
+        }
+        if (!full) break;
+        float a[kBatch][kILP], b[kBatch][kILP];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const float* __restrict__ up = U + t[u].u + r0;
+            const float* __restrict__ vp = V + t[u].v + r0;
+#pragma unroll
+            for (int j = 0; j < kILP; ++j) {
+                a[u][j] = STREAM_U ? __ldcs(up + j * kBlock) : __ldg(up + j * kBlock);
+                b[u][j] = __ldg(vp + j * kBlock);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u)
+#pragma unroll
+            for (int j = 0; j < kILP; ++j) acc[j] = mul_add_rn(acc[j], a[u][j], b[u][j]);
+    }
+    for (; q < nt; ++q) {
         const Term t = s_terms[q];
         if (t.lo <= tile_lo && tile_hi <= t.hi) {
             const float* __restrict__ up = U + t.u + r0;

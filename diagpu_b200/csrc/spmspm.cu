@@ -10,8 +10,8 @@
  *                        storage order, with an order-preserving ballot
  *                        compaction, and writes the term list (element
  *                        offsets + valid rows) to stream-ordered scratch.
- *   pair_sum_kernel   -- persistent CTAs walk (output diagonal, row tile)
- *                        work items, output diagonal fastest, so the A and B
+ *   pair_sum_kernel   -- persistent CTAs walk (output diagonal, run of row
+ *                        tiles) work items, output diagonal fastest, so the A and B
  *                        rows of one tile stay in L2 while all output
  *                        diagonals of that tile are produced.  Each output
  *                        value is accumulated in a register and stored once:
@@ -157,43 +157,91 @@ struct SumArgs {
     int nOut;
     int row_lo;
     int ntiles;
+    int tiles_per_item;  /* consecutive row tiles one work item covers */
 };
 
-template <bool ACCUM>
+/* Persistent CTAs walk work items (output diagonal c, run of tiles), c
+ * fastest.  An item loads its term list into shared memory once and then
+ * sweeps its tiles, so the descriptor/term fetch latency is paid once per
+ * tiles_per_item tiles. */
+template <bool ACCUM, int ILP, int BATCH>
 __global__ void __launch_bounds__(kBlock) pair_sum_kernel(SumArgs s)
 {
+    constexpr int kTile = kBlock * ILP;
     __shared__ Term s_t[kMaxTerms];
-    const long long items = (long long)s.nOut * s.ntiles;
+    const int nchunks = (s.ntiles + s.tiles_per_item - 1) / s.tiles_per_item;
+    const long long items = (long long)s.nOut * nchunks;
     for (long long it = blockIdx.x; it < items; it += gridDim.x) {
         const int c = (int)(it % s.nOut);
-        const int tile_lo = s.row_lo + (int)(it / s.nOut) * kTile;
+        const int tfirst = (int)(it / s.nOut) * s.tiles_per_item;
+        const int tlast = min(s.ntiles, tfirst + s.tiles_per_item);
         const OutDesc od = s.outs[c];
-        const int wlo = max(od.wlo, tile_lo), whi = min(od.whi, tile_lo + kTile);
-        if (wlo >= whi) continue;
-        const int r0 = tile_lo + (int)threadIdx.x;
-        float acc[kILP];
-#pragma unroll
-        for (int j = 0; j < kILP; ++j) acc[j] = 0.0f;
-        for (int t0 = od.t0; t0 < od.t1; t0 += kMaxTerms) {
-            const int nt = min(kMaxTerms, od.t1 - t0);
+        const int span_lo = s.row_lo + tfirst * kTile, span_hi = s.row_lo + tlast * kTile;
+        if (max(od.wlo, span_lo) >= min(od.whi, span_hi)) continue;
+        const int nt = od.t1 - od.t0;
+        const bool resident = nt <= kMaxTerms;
+        if (resident) {
             __syncthreads();
-            for (int q = threadIdx.x; q < nt; q += kBlock) s_t[q] = s.terms[t0 + q];
+            for (int q = threadIdx.x; q < nt; q += kBlock) s_t[q] = s.terms[od.t0 + q];
             __syncthreads();
-            accumulate_terms<false>(s.U, s.V, s_t, nt, tile_lo, r0, acc);
         }
+        for (int tile = tfirst; tile < tlast; ++tile) {
+            const int tile_lo = s.row_lo + tile * kTile;
+            const int wlo = max(od.wlo, tile_lo), whi = min(od.whi, tile_lo + kTile);
+            if (wlo >= whi) continue;
+            const int r0 = tile_lo + (int)threadIdx.x;
+            float acc[ILP];
 #pragma unroll
-        for (int j = 0; j < kILP; ++j) {
-            const int i = r0 + j * kBlock;
-            if (i >= wlo && i < whi) {
-                const float v = (i >= od.olo && i < od.ohi) ? acc[j] : 0.0f;
-                float* dst = s.O + od.o + i;
-                if (ACCUM)
-                    *dst = __fadd_rn(*dst, v);
-                else
-                    __stcs(dst, v);
+            for (int j = 0; j < ILP; ++j) acc[j] = 0.0f;
+            if (resident) {
+                accumulate_terms<false, ILP, BATCH>(s.U, s.V, s_t, nt, tile_lo, r0, acc);
+            } else {
+                for (int t0 = od.t0; t0 < od.t1; t0 += kMaxTerms) {
+                    const int m = min(kMaxTerms, od.t1 - t0);
+                    __syncthreads();
+                    for (int q = threadIdx.x; q < m; q += kBlock) s_t[q] = s.terms[t0 + q];
+                    __syncthreads();
+                    accumulate_terms<false, ILP, BATCH>(s.U, s.V, s_t, m, tile_lo, r0, acc);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < ILP; ++j) {
+                const int i = r0 + j * kBlock;
+                if (i >= wlo && i < whi) {
+                    const float v = (i >= od.olo && i < od.ohi) ? acc[j] : 0.0f;
+                    float* dst = s.O + od.o + i;
+                    if (ACCUM)
+                        *dst = __fadd_rn(*dst, v);
+                    else
+                        __stcs(dst, v);
+                }
             }
         }
     }
+}
+
+/* Launch the persistent pair-sum kernel over nOut output diagonals and the
+ * rows [row_lo, row_hi). */
+template <int ILP, int BATCH>
+static int launch_pair_sum_t(const float* U, const float* V, float* O, const OutDesc* outs,
+                             const Term* terms, int nOut, int row_lo, int row_hi,
+                             bool accumulate, cudaStream_t stream)
+{
+    constexpr int kTile = kBlock * ILP;
+    SumArgs s{U, V, O, outs, terms, nOut, row_lo, (row_hi - row_lo + kTile - 1) / kTile, 1};
+    const void* k = accumulate ? (const void*)pair_sum_kernel<true, ILP, BATCH>
+                               : (const void*)pair_sum_kernel<false, ILP, BATCH>;
+    const long long slots = persistent_blocks(k, 0);
+    const long long tiles = (long long)nOut * s.ntiles;
+    s.tiles_per_item = (int)std::max(1LL, std::min(16LL, tiles / (8 * slots)));
+    const int nchunks = (s.ntiles + s.tiles_per_item - 1) / s.tiles_per_item;
+    const long long grid = std::min(slots, (long long)nOut * nchunks);
+    if (accumulate)
+        pair_sum_kernel<true, ILP, BATCH><<<(unsigned)grid, kBlock, 0, stream>>>(s);
+    else
+        pair_sum_kernel<false, ILP, BATCH><<<(unsigned)grid, kBlock, 0, stream>>>(s);
+    DIA_TRY_CUDA(cudaGetLastError());
+    return DIA_OK;
 }
 
 /* Launch the persistent pair-sum kernel over nOut output diagonals and the
@@ -203,17 +251,7 @@ int launch_pair_sum(const float* U, const float* V, float* O, const OutDesc* out
                     cudaStream_t stream)
 {
     if (nOut <= 0 || row_hi <= row_lo) return DIA_OK;
-    SumArgs s{U, V, O, outs, terms, nOut, row_lo, (row_hi - row_lo + kTile - 1) / kTile};
-    const long long items = (long long)nOut * s.ntiles;
-    const void* k = accumulate ? (const void*)pair_sum_kernel<true> : (const void*)pair_sum_kernel<false>;
-    long long grid = persistent_blocks(k, 0);
-    grid = std::min(grid, items);
-    if (accumulate)
-        pair_sum_kernel<true><<<(unsigned)grid, kBlock, 0, stream>>>(s);
-    else
-        pair_sum_kernel<false><<<(unsigned)grid, kBlock, 0, stream>>>(s);
-    DIA_TRY_CUDA(cudaGetLastError());
-    return DIA_OK;
+    return launch_pair_sum_t<4, 4>(U, V, O, outs, terms, nOut, row_lo, row_hi, accumulate, stream);
 }
 
 static int run_planned(PlanArgs p, const float* U, const float* V, float* O,
