@@ -55,6 +55,7 @@ def lib():
         L.dia_spmv_rows.argtypes = [i64, i64, i, p, p, i64, i64, i64, i64, p, i64, i64, p, p]
         L.dia_spmspm_symbolic.argtypes = [i, p, i, p, i, p, p, p, p, p, p, p, p]
         L.dia_spmspm_hm.argtypes = [p, p, p, p, i, p, p, p, p, p, p, p, p, i, i, p]
+        L.dia_spmspm_hm_noalloc.argtypes = [p, p, p, p, i, p, p, p, p, p, p, p, p, i, i, p]
         L.dia_spmspm_rows.argtypes = [i64, p, i64, p, i, p, i64, i64, i64, i64, p, i, p, i64,
                                       p, i, i64, i64, i64, p]
         L.dia_gemm_diag.argtypes = [p, p, p, p, i, i, i, p, p, p, p, p]
@@ -62,7 +63,7 @@ def lib():
         L.dia_synth_rows.argtypes = [u64, i64, i64, i, p, p, i, f, f, i64, i64, i64, p, p]
         L.dia_synth_vector.argtypes = [u64, i64, i64, f, f, p, p]
         for name in ("dia_spmv_recon", "dia_spmv_rows", "dia_spmspm_symbolic", "dia_spmspm_hm",
-                     "dia_spmspm_rows", "dia_gemm_diag", "dia_gemm_diag_ex", "dia_synth_rows",
+                     "dia_spmspm_hm_noalloc", "dia_spmspm_rows", "dia_gemm_diag", "dia_gemm_diag_ex", "dia_synth_rows",
                      "dia_synth_vector"):
             getattr(L, name).restype = i
         _lib = L

@@ -343,3 +343,94 @@ extern "C" int dia_spmspm_rows(int64_t n, const float* d_A_vals, int64_t A_strid
     p.row_hi = (int)row_hi;
     return run_planned(p, d_A_vals, d_B_vals, d_C_vals, stream);
 }
+
+/* ------------------------------------------------------------------------
+ * Allocation-free variant of dia_spmspm_hm.
+ *
+ * dia_spmspm_hm takes its pair-plan scratch from the stream-ordered
+ * allocator.  Some callers cannot allocate device memory at call time: an
+ * application whose own allocator has reserved all device memory up front,
+ * a solver loop that runs under a fixed memory budget, or code that must not
+ * touch the driver's allocator while it runs.  This entry point keeps the
+ * plan in a file-scope device array instead, so it performs no allocation of
+ * any kind.  Its limit is the size of that array.
+ * ------------------------------------------------------------------------ */
+#include <mutex>
+
+namespace dia {
+
+/* 8 MiB of plan: C_ndiag * A_ndiag * 24 + C_ndiag * 32 bytes must fit. */
+constexpr size_t kStaticPlanBytes = size_t(8) << 20;
+static __device__ __align__(256) unsigned char g_static_plan[kStaticPlanBytes];
+
+/* Device address of g_static_plan on the current device, looked up once per
+ * device (the host-side symbol is only a stand-in, never a device pointer). */
+static int static_plan_address(void** out)
+{
+    constexpr int kMaxDevices = 64;
+    static std::mutex mu;
+    static void* addr[kMaxDevices] = {};
+    int dev = 0;
+    DIA_TRY_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices)
+        return fail(DIA_ERR_UNSUPPORTED, "dia_spmspm_hm_noalloc: device index above 63");
+    std::lock_guard<std::mutex> g(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        DIA_TRY_CUDA(cudaGetSymbolAddress(&p, g_static_plan));
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return DIA_OK;
+}
+
+}  // namespace dia
+
+extern "C" int dia_spmspm_hm_noalloc(const float* d_A_values, const size_t* d_A_starts,
+                                     const int* d_A_off, const int* d_A_len, int A_ndiag,
+                                     const float* d_B_values, const size_t* d_B_starts,
+                                     const int* d_B_len, const int* d_B_lookup,
+                                     float* d_C_values, const size_t* d_C_starts,
+                                     const int* d_C_off, const int* d_C_len, int C_ndiag, int n,
+                                     cudaStream_t stream)
+{
+    if (n < 0 || A_ndiag < 0 || C_ndiag < 0)
+        return fail(DIA_ERR_INVALID, "dia_spmspm_hm_noalloc: negative size");
+    if (n == 0 || C_ndiag == 0) return DIA_OK;
+    if (!d_C_values || !d_C_starts || !d_C_off || !d_C_len ||
+        (A_ndiag > 0 && (!d_A_values || !d_A_starts || !d_A_off || !d_A_len || !d_B_values ||
+                         !d_B_starts || !d_B_len || !d_B_lookup)))
+        return fail(DIA_ERR_INVALID, "dia_spmspm_hm_noalloc: null pointer");
+    if ((long long)n + kTile >= (1LL << 31))
+        return fail(DIA_ERR_UNSUPPORTED, "dia_spmspm_hm_noalloc: n beyond int32 range");
+    const int stride_terms = std::max(A_ndiag, 1);
+    const size_t term_bytes = (size_t)C_ndiag * stride_terms * sizeof(Term);
+    const size_t need = term_bytes + (size_t)C_ndiag * sizeof(OutDesc);
+    if (need > kStaticPlanBytes)
+        return fail(DIA_ERR_CAPACITY,
+                    "dia_spmspm_hm_noalloc: plan needs " + std::to_string(need) +
+                        " bytes (C_ndiag * A_ndiag * 24 + C_ndiag * 32) but the static buffer "
+                        "holds " + std::to_string(kStaticPlanBytes) + "; use dia_spmspm_hm");
+    void* ws = nullptr;
+    const int rc = static_plan_address(&ws);
+    if (rc != DIA_OK) return rc;
+    PlanArgs p{};
+    p.A = LayoutDesc{1, d_A_off, d_A_starts, nullptr, d_A_len, 0, 0, 0, 0, n};
+    p.B = LayoutDesc{1, nullptr, d_B_starts, nullptr, d_B_len, 0, 0, 0, 0, n};
+    p.C = LayoutDesc{1, d_C_off, d_C_starts, nullptr, d_C_len, 0, 0, 0, 0, n};
+    p.nA = A_ndiag;
+    p.nB = 0;
+    p.nC = C_ndiag;
+    p.B_lookup = d_B_lookup;
+    p.row_lo = 0;
+    p.row_hi = n;
+    p.stride_terms = stride_terms;
+    /* every descriptor and every term the sum kernel reads is rewritten by
+     * the plan kernel first, so nothing left by an earlier call is used */
+    p.terms = (Term*)ws;
+    p.outs = (OutDesc*)((char*)ws + term_bytes);
+    pair_plan_kernel<<<std::min(C_ndiag, 8 * num_sms()), kBlock, 0, stream>>>(p);
+    DIA_TRY_CUDA(cudaGetLastError());
+    return launch_pair_sum(d_A_values, d_B_values, d_C_values, p.outs, p.terms, C_ndiag, 0, n,
+                           false, stream);
+}

@@ -103,6 +103,25 @@ int dia_spmspm_hm(const float* d_A_values, const size_t* d_A_starts,
                   const int* d_C_off, const int* d_C_len, int C_ndiag, int n,
                   cudaStream_t stream);
 
+/* dia_spmspm_hm without any device allocation.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory while
+ * they run (an allocator that reserved all device memory up front, a fixed
+ * memory budget, code that must not enter the driver's allocator).  The pair
+ * plan lives in a library-owned 8 MiB device array, held on every GPU that
+ * loads the library until the process exits, so C_ndiag * A_ndiag * 24 +
+ * C_ndiag * 32 must not exceed 8 MiB (DIA_ERR_CAPACITY otherwise).  The
+ * first call on a device looks up that array's device address, so make it
+ * before any stream capture.  All calls share the one array: calls whose
+ * work overlaps on the GPU (other streams, other host threads) race; order
+ * them on one stream.  Results equal dia_spmspm_hm bit for bit. */
+int dia_spmspm_hm_noalloc(const float* d_A_values, const size_t* d_A_starts,
+                          const int* d_A_off, const int* d_A_len, int A_ndiag,
+                          const float* d_B_values, const size_t* d_B_starts,
+                          const int* d_B_len, const int* d_B_lookup,
+                          float* d_C_values, const size_t* d_C_starts,
+                          const int* d_C_off, const int* d_C_len, int C_ndiag, int n,
+                          cudaStream_t stream);
+
 /* C = A*B on the rows layout (A and C share vrow0 and the output rows
  * [row_lo, row_hi); B holds global rows [b_lo, b_hi) at B_vals[k*B_stride +
  * r - b_vrow0], i.e. a row block plus its halo).  C rows in [row_lo, row_hi)
