@@ -60,6 +60,8 @@ def lib():
                                       p, i, i64, i64, i64, p]
         L.dia_gemm_diag.argtypes = [p, p, p, p, i, i, i, p, p, p, p, p]
         L.dia_gemm_diag_ex.argtypes = [p, p, p, p, p, p, i, i, i, p, p, p, p, i, i, p]
+        L.dia_device_status.argtypes = [p, i]
+        L.dia_device_status.restype = i
         L.dia_synth_rows.argtypes = [u64, i64, i64, i, p, p, i, f, f, i64, i64, i64, p, p]
         L.dia_synth_vector.argtypes = [u64, i64, i64, f, f, p, p]
         for name in ("dia_spmv_recon", "dia_spmv_rows", "dia_spmspm_symbolic", "dia_spmspm_hm",
@@ -295,3 +297,10 @@ def gemm_diag_layout(n, off_A, off_B):
     k2i[k_list + n - 1] = np.arange(len(k_list), dtype=np.int32)
     total = int(sym["C_len"].astype(np.int64).sum())
     return starts.astype(np.int32), sym["C_len"], k2i, k_list, total
+
+
+def device_status(clear=True):
+    """Status bits set by kernels that gave up a bounded wait (0 = none)."""
+    v = C.c_uint(0)
+    check(lib().dia_device_status(C.byref(v), int(clear)))
+    return v.value

@@ -166,6 +166,14 @@ int dia_gemm_diag_ex(const float* d_DA, const float* d_DB, const int* d_off_A,
                      const int* d_k_to_idx, int beta, int mode,
                      cudaStream_t stream);
 
+/* Device status word shared by the library's kernels.  Kernels that wait on
+ * the hardware (the tcgen05 dense-band kernel's mbarrier waits) never spin
+ * without bound: on giving up they set a bit here and return early.  Reads
+ * the word into *flags (synchronous); clear != 0 resets it.  No counterpart
+ * in the reference, whose kernels have no waits. */
+enum { DIA_TC_TIMEOUT = 1 };
+int dia_device_status(unsigned int* flags, int clear);
+
 /* ------------------------------------------------ synthetic test inputs */
 
 /* Fill rows [row0, row0+nrows) of a rows-layout matrix (K diagonals, stride)

@@ -88,3 +88,43 @@ def test_config4_dense_band(mode):
     ref64, _ = oracle.gemm_diag(DA.cpu().numpy(), off, DB.cpu().numpy(), off, n, f64=True)
     err = rel_l2(got, ref64)
     assert err <= (1e-6 if mode == dg.GEMM_SIMT else TF32_TOL), err
+
+
+@pytest.mark.parametrize("n,lo_a,P,lo_b,Q", [(256, -4, 9, -4, 9), (1000, -64, 129, -64, 129),
+                                            (777, -3, 5, 2, 40), (130, 0, 1, 0, 1),
+                                            (5000, -20, 41, -100, 120)])
+def test_tcgen05_small_bands(n, lo_a, P, lo_b, Q):
+    """Tensor-core mode on contiguous bands: ragged last tile, asymmetric
+    and one-diagonal bands, the widest supported B band."""
+    offA = np.arange(lo_a, lo_a + P, dtype=np.int32)
+    offB = np.arange(lo_b, lo_b + Q, dtype=np.int32)
+    DA = dg.DiaRows.synth(n, n, offA, seed=11).vals[:, :n].contiguous()
+    DB = dg.DiaRows.synth(n, n, offB, seed=12).vals[:, :n].contiguous()
+    co, cl, k2i, kl, tot = oracle.build_c_layout(n, offA, offB)
+    for beta in (0, 1):
+        C0 = torch.full((tot,), 0.5, device="cuda")
+        dg.gemm_diag(DA, DB, dev(offA), dev(offB), n, C0, dev(co), dev(cl), dev(k2i),
+                     mode=dg.GEMM_TCGEN05, beta=beta)
+        torch.cuda.synchronize()
+        assert dg.device_status() == 0
+        ref = np.zeros(tot, np.float64)
+        oracle.lib().orc_gemm_diag_f64(DA.cpu().numpy().reshape(-1), offA, P,
+                                       DB.cpu().numpy().reshape(-1), offB, Q, n, ref, co, k2i,
+                                       oracle.threads())
+        got = C0.cpu().numpy().astype(np.float64) - (0.5 if beta else 0.0)
+        assert rel_l2(got, ref) <= TF32_TOL, (beta, rel_l2(got, ref))
+
+
+def test_tcgen05_rejects_wide_bands_auto_falls_back():
+    n = 2000
+    off = np.arange(-150, 151, dtype=np.int32)          # P + Q - 1 = 601 > 257
+    DA = dg.DiaRows.synth(n, n, off, seed=1).vals[:, :n].contiguous()
+    co, cl, k2i, kl, tot = oracle.build_c_layout(n, off, off)
+    C = torch.zeros(tot, device="cuda")
+    with pytest.raises(dg.DiaError) as e:
+        dg.gemm_diag(DA, DA, dev(off), dev(off), n, C, dev(co), dev(cl), dev(k2i),
+                     mode=dg.GEMM_TCGEN05)
+    assert e.value.code == dg.DIA_ERR_UNSUPPORTED
+    dg.gemm_diag(DA, DA, dev(off), dev(off), n, C, dev(co), dev(cl), dev(k2i), beta=0)
+    ref = oracle.gemm_diag(DA.cpu().numpy(), off, DA.cpu().numpy(), off, n, f64=False)[0]
+    assert same(C.cpu().numpy(), ref)   # AUTO took the exact SIMT path
