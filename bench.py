@@ -191,8 +191,9 @@ def roofline(achieved_gbs, hbm, src, traffic=None):
 
 def secondary_spmspm(dg, name, n, A, B, steps, warmup, hbm, src, flush=None):
     sym = dg.spmspm_symbolic(n, A.offsets, B.offsets)
-    Cm = dg.DiaRows.empty(n, n, sym["C_off"], device="cuda", zero=True)
-    fn = lambda: dg.spmspm(A, B, Cm, symbolic=sym)
+    plan = dg.SpmspmPlan(A, B)
+    Cm = plan.new_C()
+    fn = lambda: plan.execute(A, B, Cm)
     ms = timed(fn, steps, warmup, flush=flush, per_launch=flush is not None)
     nnzA = nnz_rows(n, A.offsets, 0, n)
     nnzB = 0 if B is A else nnz_rows(n, B.offsets, 0, n)
@@ -477,10 +478,12 @@ def _only_spmspm(dg, n, offsA, offsB=None, kind=0):
     B = A if offsB is None else dg.DiaRows.synth(n, n, offsB, SEED_X, kind=kind,
                                                   lo=-1.0 if kind == 0 else 0.0)
     sym = dg.spmspm_symbolic(n, A.offsets, B.offsets)
-    Cm = dg.DiaRows.empty(n, n, sym["C_off"], zero=True)
+    plan = dg.SpmspmPlan(A, B)
+    Cm = plan.new_C()
     byts = 4 * (nnz_rows(n, A.offsets, 0, n) + (0 if B is A else nnz_rows(n, B.offsets, 0, n))
                 + int(sym["C_len"].astype(np.int64).sum()))
-    return (lambda: dg.spmspm(A, B, Cm, symbolic=sym)), byts
+    tiles = os.environ.get("DIA_BENCH_TILES", "1") == "1"
+    return (lambda: plan.execute(A, B, Cm, use_tiles=tiles)), byts
 
 
 def _scat(seed):

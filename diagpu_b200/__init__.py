@@ -60,6 +60,14 @@ def lib():
                                       p, i, i64, i64, i64, p]
         L.dia_gemm_diag.argtypes = [p, p, p, p, i, i, i, p, p, p, p, p]
         L.dia_gemm_diag_ex.argtypes = [p, p, p, p, p, p, i, i, i, p, p, p, p, i, i, p]
+        L.dia_spmspm_plan_create.argtypes = [i64, p, i, p, i, i64, i64, i64, i64, i64, i64, i64,
+                                             i64, p]
+        L.dia_spmspm_plan_info.argtypes = [p, p, p, p, p, p, p, p]
+        L.dia_spmspm_plan_execute.argtypes = [p, p, p, p, i64, i64, i, p]
+        L.dia_spmspm_plan_destroy.argtypes = [p]
+        for name in ("dia_spmspm_plan_create", "dia_spmspm_plan_info", "dia_spmspm_plan_execute",
+                     "dia_spmspm_plan_destroy"):
+            getattr(L, name).restype = i
         L.dia_device_status.argtypes = [p, i]
         L.dia_device_status.restype = i
         L.dia_synth_rows.argtypes = [u64, i64, i64, i, p, p, i, f, f, i64, i64, i64, p, p]
@@ -247,11 +255,69 @@ def spmspm_hm(A_values, A_starts, A_off, A_len, B_values, B_starts, B_len, B_loo
     return C_values
 
 
+class SpmspmPlan:
+    """Reusable plan for C = A*B on the rows layout (dia_spmspm_plan_*).
+
+    Fixes the offsets and buffer geometry of A (rows [A.vrow0, +A.nrows)),
+    B (rows [b_lo, b_hi) of the block B) and C (same rows as A).  Creating it
+    runs the symbolic phase and uploads the tables; execute() launches only
+    kernels (the shared-memory-tiled kernel on the interior rows when the
+    offsets allow it, the generic kernel elsewhere)."""
+
+    def __init__(self, A: DiaRows, B: DiaRows, *, b_lo=None, b_hi=None):
+        b_lo = B.vrow0 if b_lo is None else b_lo
+        b_hi = B.vrow0 + B.nrows if b_hi is None else b_hi
+        self._h = C.c_void_p()
+        a_off = np.ascontiguousarray(A.offsets, np.int32)
+        b_off = np.ascontiguousarray(B.offsets, np.int32)
+        pa = lambda x: x.ctypes.data_as(C.c_void_p)
+        with torch.cuda.device(A.vals.device):
+            check(lib().dia_spmspm_plan_create(A.n_rows, pa(a_off), len(a_off), pa(b_off),
+                                               len(b_off), A.stride, B.stride, A.stride,
+                                               A.vrow0, A.nrows, B.vrow0, b_lo, b_hi,
+                                               C.byref(self._h)))
+        nc = C.c_int(0)
+        check(lib().dia_spmspm_plan_info(self._h, C.byref(nc), None, None, None, None, None,
+                                         None))
+        self.C_off = np.empty(nc.value, np.int32)
+        tr, tlo, thi = C.c_int(0), C.c_int64(0), C.c_int64(0)
+        check(lib().dia_spmspm_plan_info(self._h, None, pa(self.C_off), None, None,
+                                         C.byref(tr), C.byref(tlo), C.byref(thi)))
+        self.tile_rows, self.tiled = tr.value, (tlo.value, thi.value)
+        self.A, self.B = A, B
+
+    def new_C(self, zero=True):
+        A = self.A
+        return DiaRows.empty(A.n_rows, A.n_cols, self.C_off, vrow0=A.vrow0, nrows=A.nrows,
+                             device=A.vals.device, zero=zero)
+
+    def execute(self, A, B, C_out, row_lo=None, row_hi=None, *, use_tiles=True, stream=None):
+        lo = A.vrow0 if row_lo is None else row_lo
+        hi = A.vrow0 + A.nrows if row_hi is None else row_hi
+        check(lib().dia_spmspm_plan_execute(self._h, _dptr(A.vals), _dptr(B.vals),
+                                            _dptr(C_out.vals), lo, hi, int(use_tiles),
+                                            _stream(stream)))
+        return C_out
+
+    def __del__(self):
+        if getattr(self, "_h", None) and self._h.value and _lib is not None:
+            _lib.dia_spmspm_plan_destroy(self._h)
+            self._h = C.c_void_p()
+
+
 def spmspm(A: DiaRows, B: DiaRows, C_out: DiaRows | None = None, *, b_lo=None, b_hi=None,
-           symbolic=None, stream=None):
+           symbolic=None, method="auto", stream=None):
     """C = A*B on the rows layout.  A and C cover the same row block; B may
-    be a wider block (the halo rows of a partitioned product)."""
+    be a wider block (the halo rows of a partitioned product).
+    method: "auto"/"tiled" plan the product (tiled kernel where possible),
+    "planned_generic" plans it but keeps the generic kernel, "generic" runs
+    the unplanned entry point (device-side pair resolution)."""
     n = A.n_rows
+    if method != "generic":
+        plan = SpmspmPlan(A, B, b_lo=b_lo, b_hi=b_hi)
+        if C_out is None:
+            C_out = plan.new_C()
+        return plan.execute(A, B, C_out, use_tiles=method != "planned_generic", stream=stream)
     if symbolic is None:
         symbolic = spmspm_symbolic(n, A.offsets, B.offsets)
     if C_out is None:

@@ -156,6 +156,7 @@ struct SumArgs {
     const Term* terms;
     int nOut;
     int row_lo;
+    int row_hi;
     int ntiles;
     int tiles_per_item;  /* consecutive row tiles one work item covers */
 };
@@ -187,7 +188,8 @@ __global__ void __launch_bounds__(kBlock) pair_sum_kernel(SumArgs s)
         }
         for (int tile = tfirst; tile < tlast; ++tile) {
             const int tile_lo = s.row_lo + tile * kTile;
-            const int wlo = max(od.wlo, tile_lo), whi = min(od.whi, tile_lo + kTile);
+            const int wlo = max(od.wlo, tile_lo);
+            const int whi = min(min(od.whi, tile_lo + kTile), s.row_hi);
             if (wlo >= whi) continue;
             const int r0 = tile_lo + (int)threadIdx.x;
             float acc[ILP];
@@ -228,7 +230,7 @@ static int launch_pair_sum_t(const float* U, const float* V, float* O, const Out
                              bool accumulate, cudaStream_t stream)
 {
     constexpr int kTile = kBlock * ILP;
-    SumArgs s{U, V, O, outs, terms, nOut, row_lo, (row_hi - row_lo + kTile - 1) / kTile, 1};
+    SumArgs s{U, V, O, outs, terms, nOut, row_lo, row_hi, (row_hi - row_lo + kTile - 1) / kTile, 1};
     const void* k = accumulate ? (const void*)pair_sum_kernel<true, ILP, BATCH>
                                : (const void*)pair_sum_kernel<false, ILP, BATCH>;
     const long long slots = persistent_blocks(k, 0);
@@ -274,6 +276,37 @@ static int run_planned(PlanArgs p, const float* U, const float* V, float* O,
     cudaError_t ef = cudaFreeAsync(ws, stream);
     if (rc == DIA_OK && ef != cudaSuccess) rc = cuda_fail(ef, "cudaFreeAsync");
     return rc;
+}
+
+/* Term lists of a rows-layout product written into caller buffers
+ * (terms: nC * nA slots, outs: nC), for plans that keep them. */
+int build_generic_terms_rows(long long n, const int* d_A_off, int nA, const int* d_B_off, int nB,
+                             const int* d_C_off, int nC, long long A_stride,
+                             long long B_stride, long long b_vrow0, long long b_lo,
+                             long long b_hi, long long C_stride, long long vrow0,
+                             long long row_lo, long long row_hi, Term* terms, OutDesc* outs,
+                             cudaStream_t stream)
+{
+    const int in = (int)n;
+    PlanArgs p{};
+    p.A = LayoutDesc{0, d_A_off, nullptr, nullptr, nullptr, A_stride, vrow0, (int)vrow0,
+                     (int)std::min<long long>(vrow0 + A_stride, n), in};
+    p.B = LayoutDesc{0, d_B_off, nullptr, nullptr, nullptr, B_stride, b_vrow0,
+                     (int)std::max<long long>(b_lo, 0), (int)std::min<long long>(b_hi, n), in};
+    p.C = LayoutDesc{0, d_C_off, nullptr, nullptr, nullptr, C_stride, vrow0, (int)vrow0,
+                     (int)std::min<long long>(vrow0 + C_stride, n), in};
+    p.nA = nA;
+    p.nB = nB;
+    p.nC = nC;
+    p.B_off = d_B_off;
+    p.row_lo = (int)row_lo;
+    p.row_hi = (int)row_hi;
+    p.stride_terms = std::max(nA, 1);
+    p.terms = terms;
+    p.outs = outs;
+    pair_plan_kernel<<<std::min(nC, 8 * num_sms()), kBlock, 0, stream>>>(p);
+    DIA_TRY_CUDA(cudaGetLastError());
+    return DIA_OK;
 }
 
 }  // namespace dia

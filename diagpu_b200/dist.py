@@ -21,7 +21,7 @@ import numpy as np
 import torch
 import torch.distributed as dist
 
-from . import DiaRows, round_stride, spmspm, spmspm_symbolic, spmv
+from . import DiaRows, SpmspmPlan, spmspm_symbolic, spmv
 
 
 def row_block(n: int, world: int, rank: int, align: int = 32):
@@ -158,38 +158,34 @@ class DistSpmv:
 
 class DistSpmspm:
     """C = A*B with A, B, C row-partitioned; B's halo rows (within max|d_A|
-    of the block) come from the neighbours."""
+    of the block) come from the neighbours.  Two plans: one whose B range is
+    this rank's own rows (interior rows, run while the halo is in flight)
+    and one over the whole halo window (boundary rows, run after it)."""
 
     def __init__(self, A: DiaRows, B_ext: DiaRows, halo: Halo, group=None):
         self.A, self.B, self.halo, self.group = A, B_ext, halo, group
+        h = halo
+        self.plan_own = SpmspmPlan(A, B_ext, b_lo=h.r0, b_hi=h.r1)
+        self.plan_all = SpmspmPlan(A, B_ext, b_lo=h.xlo, b_hi=h.xhi)
+        self.C = self.plan_all.new_C()
         self.sym = spmspm_symbolic(A.n_rows, A.offsets, B_ext.offsets)
-        self.C = DiaRows.empty(A.n_rows, A.n_cols, self.sym["C_off"], vrow0=A.vrow0,
-                               nrows=A.nrows, device=A.vals.device, zero=True)
 
     def step(self, launches: list | None = None):
         h = self.halo
         pend = h.start(self.B.vals, self.group) if h.world > 1 else None
-        # interior rows: all B rows they touch are this rank's own
         a, b = h.interior()
+        plan_in = self.plan_all if pend is None else self.plan_own
         if b > a:
-            self._rows(a, b, h.r0, h.r1)
+            plan_in.execute(self.A, self.B, self.C, a, b)
             if launches is not None:
-                launches += ["pair_plan", "pair_sum"]
+                launches += ["tile_sum", "pair_sum"]
         if pend is not None:
             pend.wait()
         for lo, hi in h.boundary():
-            self._rows(lo, hi, h.xlo, h.xhi)
+            self.plan_all.execute(self.A, self.B, self.C, lo, hi)
             if launches is not None:
-                launches += ["pair_plan", "pair_sum"]
+                launches += ["pair_sum"]
         return self.C
-
-    def _rows(self, lo, hi, b_lo, b_hi):
-        from . import _dptr, _stream, check, lib
-        A, B, Cm = self.A, self.B, self.C
-        check(lib().dia_spmspm_rows(A.n_rows, _dptr(A.vals), A.stride, _dptr(A.d_offsets), A.K,
-                                    _dptr(B.vals), B.stride, B.vrow0, b_lo, b_hi,
-                                    _dptr(B.d_offsets), B.K, _dptr(Cm.vals), Cm.stride,
-                                    _dptr(Cm.d_offsets), Cm.K, A.vrow0, lo, hi, _stream()))
 
 
 def offsets_span(offsets):

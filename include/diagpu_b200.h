@@ -136,6 +136,33 @@ int dia_spmspm_rows(int64_t n, const float* d_A_vals, int64_t A_stride,
                     int64_t vrow0, int64_t row_lo, int64_t row_hi,
                     cudaStream_t stream);
 
+/* Planned C = A*B on the rows layout (the analogue of the reference's
+ * host Schedule, spmspm/bench_spmspm.cu:137-243, built once and reused).
+ * The plan fixes the offsets and the buffer geometry: A and C hold rows
+ * [vrow0, vrow0 + nrows) with strides A_stride / C_stride, B holds global
+ * rows [b_lo, b_hi) at B_vals[k*B_stride + r - b_vrow0].  It runs the
+ * symbolic phase, uploads its tables (cudaMalloc, owned by the plan) and,
+ * when A's offsets cluster tightly enough for the operands of a row tile to
+ * fit in shared memory, enables the tiled kernel for the interior rows.
+ * C offsets come back through dia_spmspm_plan_info. */
+typedef struct DiaSpmspmPlan DiaSpmspmPlan;
+int dia_spmspm_plan_create(int64_t n, const int* h_A_off, int nA, const int* h_B_off,
+                           int nB, int64_t A_stride, int64_t B_stride, int64_t C_stride,
+                           int64_t vrow0, int64_t nrows, int64_t b_vrow0, int64_t b_lo,
+                           int64_t b_hi, DiaSpmspmPlan** plan);
+/* Output structure (any pointer may be NULL), tile rows of the tiled path
+ * (0: not used) and the row range it covers. */
+int dia_spmspm_plan_info(const DiaSpmspmPlan* plan, int* n_c, int* h_C_off, int* h_C_len,
+                         int64_t* h_C_start, int* tile_rows, int64_t* tiled_lo,
+                         int64_t* tiled_hi);
+/* C rows [row_lo, row_hi) of the plan's block (overwritten); use_tiles 0
+ * forces the generic kernel.  Results are identical either way.  No
+ * allocation, no synchronisation. */
+int dia_spmspm_plan_execute(const DiaSpmspmPlan* plan, const float* d_A_vals,
+                            const float* d_B_vals, float* d_C_vals, int64_t row_lo,
+                            int64_t row_hi, int use_tiles, cudaStream_t stream);
+int dia_spmspm_plan_destroy(DiaSpmspmPlan* plan);
+
 /* ----------------------------------------------------------- gemm_diag */
 
 /* C += A*B with gemm_diag_kernel's argument set (gemm_diag/gemm_diag.cu:

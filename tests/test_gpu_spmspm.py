@@ -172,3 +172,38 @@ def _window_oracle(n, offs, W, wlo, lo, hi, C_off):
             acc = np.where(ok, acc + prod, acc).astype(np.float32)
         out[c] = np.where(valid_c, acc, 0)
     return out
+
+
+@pytest.mark.parametrize("case", ["stencil7", "stencil27", "band", "scatter", "tiny"])
+def test_tiled_plan_equals_generic(case):
+    """The shared-memory-tiled path, the planned generic path and the
+    unplanned entry point give identical results (and the tiled kernel is
+    actually used where the offsets allow it)."""
+    if case == "stencil7":
+        n, offs = 64 ** 3, np.array([-4096, -64, -1, 0, 1, 64, 4096], np.int32)
+    elif case == "stencil27":
+        n = 64 * 64 * 64
+        offs = np.array([i + 64 * j + 4096 * k for k in (-1, 0, 1) for j in (-1, 0, 1)
+                         for i in (-1, 0, 1)], np.int32)
+    elif case == "band":
+        n, offs = 100_003, np.arange(-9, 10, dtype=np.int32)
+    elif case == "scatter":
+        n, offs = 300_000, _scatter_offsets(5)
+    else:
+        n, offs = 300, np.array([-2, 0, 1], np.int32)
+    A = dg.DiaRows.synth(n, n, offs, seed=71)
+    B = dg.DiaRows.synth(n, n, offs[::-1].copy(), seed=72)
+    plan = dg.SpmspmPlan(A, B)
+    if case in ("stencil7", "band"):
+        assert plan.tile_rows > 0 and plan.tiled[1] > plan.tiled[0]
+    Ct = plan.execute(A, B, plan.new_C())
+    Cg = plan.execute(A, B, plan.new_C(), use_tiles=False)
+    Cu = dg.spmspm(A, B, method="generic")
+    assert np.array_equal(plan.C_off, Cu.offsets)
+    ht, hg, hu = (x.vals.cpu().numpy() for x in (Ct, Cg, Cu))
+    assert same(ht, hu) and same(hg, hu)
+    # sub-ranges of rows, as the partitioned path calls them
+    Cs = plan.new_C()
+    for lo, hi in ((0, 1000), (1000, n // 2 + 7), (n // 2 + 7, n)):
+        plan.execute(A, B, Cs, lo, hi)
+    assert same(Cs.vals.cpu().numpy(), hu)
