@@ -27,7 +27,7 @@ namespace dia {
 
 int launch_pair_sum(const float* U, const float* V, float* O, const OutDesc* outs,
                     const Term* terms, int nOut, int row_lo, int row_hi, bool accumulate,
-                    cudaStream_t stream);
+                    cudaStream_t stream, float avg_terms = -1.0f);
 int gemm_diag_tc_supported(const int* h_off_A, int P, const int* h_off_B, int Q, int n);
 int gemm_diag_tc_launch(const float* d_DA, const float* d_DB, const int* h_off_A, int P,
                         const int* h_off_B, int Q, int n, float* d_C_data,
@@ -151,7 +151,8 @@ static int gemm_diag_simt(const float* d_DA, const float* d_DB, const int* d_off
         if (e != cudaSuccess) rc = cuda_fail(e, "gemm_plan_kernel launch");
     }
     if (rc == DIA_OK)
-        rc = launch_pair_sum(d_DA, d_DB, d_C, g.outs, g.terms, nOut, 0, n, beta != 0, stream);
+        rc = launch_pair_sum(d_DA, d_DB, d_C, g.outs, g.terms, nOut, 0, n, beta != 0, stream,
+                             (float)np / nOut);
     /* the host int buffer must outlive the copy: wait for it */
     cudaError_t es = cudaStreamSynchronize(stream);
     cudaError_t ef = cudaFreeAsync(ws, stream);

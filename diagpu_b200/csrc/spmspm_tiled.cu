@@ -32,7 +32,7 @@ namespace dia {
 
 int launch_pair_sum(const float* U, const float* V, float* O, const OutDesc* outs,
                     const Term* terms, int nOut, int row_lo, int row_hi, bool accumulate,
-                    cudaStream_t stream);
+                    cudaStream_t stream, float avg_terms = -1.0f);
 
 constexpr int kClusterSpan = 64;       /* max span of one A-offset cluster */
 constexpr int kTileSmemCap = 100 * 1024;
@@ -129,6 +129,7 @@ struct DiaSpmspmPlan {
     Term* d_gterms = nullptr;
     OutDesc* d_gouts = nullptr;
     int* d_offs = nullptr;   /* A | B | C offsets on the device */
+    float avg_terms = -1.0f; /* pairs per output diagonal */
 };
 
 namespace {
@@ -185,6 +186,7 @@ extern "C" int dia_spmspm_plan_create(int64_t n, const int* h_A_off, int nA, con
     P->b_lo = (int)std::max<int64_t>(b_lo, 0); P->b_hi = (int)std::min<int64_t>(b_hi, n);
     P->rows_lo = (int)vrow0; P->rows_hi = (int)std::min<int64_t>(vrow0 + nrows, n);
     P->C_off.resize(nc); P->C_len.resize(nc); P->C_start.resize(nc);
+    P->avg_terms = nc > 0 ? (float)np / nc : -1.0f;
     std::vector<int> ptr(nc + 1), pa(std::max<int64_t>(np, 1)), pb(std::max<int64_t>(np, 1));
     rc = dia_spmspm_symbolic((int)n, h_A_off, nA, h_B_off, nB, &nc, P->C_off.data(),
                              P->C_len.data(), (int64_t*)P->C_start.data(), &np, ptr.data(),
@@ -384,10 +386,10 @@ extern "C" int dia_spmspm_plan_execute(const DiaSpmspmPlan* P, const float* d_A_
     const float* U = d_A_vals;
     if (tlo > row_lo)
         rc = launch_pair_sum(U, d_B_vals, d_C_vals, P->d_gouts, P->d_gterms, P->nC, (int)row_lo,
-                             (int)tlo, false, stream);
+                             (int)tlo, false, stream, P->avg_terms);
     if (rc == DIA_OK && row_hi > thi)
         rc = launch_pair_sum(U, d_B_vals, d_C_vals, P->d_gouts, P->d_gterms, P->nC, (int)thi,
-                             (int)row_hi, false, stream);
+                             (int)row_hi, false, stream, P->avg_terms);
     return rc;
 }
 
