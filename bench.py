@@ -41,6 +41,10 @@ OFF5 = np.array([i + 256 * j + 65536 * k for k in (-1, 0, 1) for j in (-1, 0, 1)
                  for i in (-1, 0, 1)], np.int32)
 SEED_A, SEED_X = 5001, 5002
 REF_SAMPLE_ROWS = 4 * 1024 * 1024
+# DRAM bytes (read + write) of one spmv_kernel launch on config 5: the ncu
+# capture of the 4,194,304-row case (profiles/spmv_kernel_config5.md,
+# 471.4 MB) scaled by the ratio of algorithmic bytes (16.15)
+SPMV5_TRAFFIC = 7_611_000_000
 
 
 def peaks():
@@ -396,7 +400,8 @@ def run_ours(args):
                        "n": N5, "diagonals": 27, "nnz": nnz, "bytes_per_step": total_bytes,
                        "parallelism": f"row-block x{world}, NCCL x halo +-65793",
                        "l2": "inputs 7.8 GB > 126 MB L2 (no flush needed)"},
-            "roofline": roofline(rank_bytes / kms / 1e6, hbm, src),
+            "roofline": roofline(rank_bytes / kms / 1e6, hbm, src,
+                                 traffic=SPMV5_TRAFFIC if world == 1 else None),
             "kernel_ms": round(kms, 5),
             "cpu_baseline": cpu,
             "e2e": {"value": round(total_bytes / ems / 1e6, 1), "unit": "GB/s",
