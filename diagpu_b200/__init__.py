@@ -68,6 +68,18 @@ def lib():
         for name in ("dia_spmspm_plan_create", "dia_spmspm_plan_info", "dia_spmspm_plan_execute",
                      "dia_spmspm_plan_destroy"):
             getattr(L, name).restype = i
+        L.dia_nccl_unique_id.argtypes = [p, i]
+        L.dia_dist_create.argtypes = [i, i, p, p]
+        L.dia_dist_halo_start.argtypes = [p, p, i64, i64, i, p, p]
+        L.dia_dist_halo_wait.argtypes = [p, p]
+        L.dia_dist_spmv_step.argtypes = [p, i64, i64, i, p, p, i64, i64, p, i64, i64, p, p, i64,
+                                         i64, i64, i64, i, p]
+        L.dia_dist_async_error.argtypes = [p]
+        L.dia_dist_destroy.argtypes = [p]
+        for name in ("dia_nccl_unique_id", "dia_dist_create", "dia_dist_halo_start",
+                     "dia_dist_halo_wait", "dia_dist_spmv_step", "dia_dist_async_error",
+                     "dia_dist_destroy"):
+            getattr(L, name).restype = i
         L.dia_device_status.argtypes = [p, i]
         L.dia_device_status.restype = i
         L.dia_synth_rows.argtypes = [u64, i64, i64, i, p, p, i, f, f, i64, i64, i64, p, p]

@@ -12,7 +12,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libdiagpu_b200.so")
 SOURCES = ["status.cu", "spmv.cu", "spmspm.cu", "spmspm_tiled.cu", "symbolic.cu", "gemm_diag.cu",
-           "gemm_diag_tc.cu", "synth.cu"]
+           "gemm_diag_tc.cu", "synth.cu", "dist.cu"]
 NVCC = os.environ.get("NVCC", "nvcc")
 FLAGS = ["-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo",
          "-Xcompiler", "-fPIC", "-Xptxas", "-O3", "--expt-relaxed-constexpr",
@@ -43,7 +43,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
             subprocess.run(cmd, check=True)
     if force or _stale(LIB, objs):
         cmd = [NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-ccbin",
-               "/usr/bin/g++", *objs, "-o", LIB]
+               "/usr/bin/g++", *objs, "-o", LIB, "-lnccl"]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)

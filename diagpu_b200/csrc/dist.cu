@@ -1,0 +1,224 @@
+/*
+ * dist.cu -- native NCCL halo exchange for row-partitioned products.
+ *
+ * One process per GPU; each rank owns a contiguous row block.  Before a
+ * product, a rank needs the columns (x entries, or B rows) within the
+ * largest offset of its block boundaries from its two neighbours.  This
+ * file owns an NCCL communicator (created from a unique id the caller
+ * distributes once, e.g. through torch.distributed) and a private stream:
+ *   halo_start: the private stream waits for the caller's stream, then one
+ *               ncclGroupStart/End posts every send/receive with ranks r-1
+ *               and r+1 (one pair per stored row of the exchanged buffer);
+ *   halo_wait:  the caller's stream waits for the exchange.
+ * dia_dist_spmv_step enqueues a whole partitioned SpMV with one host call.
+ * In its default mode the halo stream has the highest priority: NCCL's
+ * transfer and then the two boundary strips run there, concurrently with
+ * the interior rows' kernel (local columns only) on the caller's stream,
+ * and their CTAs are dispatched ahead of the interior kernel's pending
+ * ones.  Measured on 8 B200s (config 5): 0.166 ms per step against 0.185
+ * ms for exchange-then-one-launch and 0.211 ms for boundary strips after
+ * the interior on one stream.
+ * The reference has no multi-GPU path (its programs run on one device).
+ */
+#include <nccl.h>
+
+#include <cstring>
+#include <string>
+
+#include "../../include/diagpu_b200.h"
+#include "dia_core.cuh"
+
+struct DiaDist {
+    ncclComm_t comm = nullptr;
+    cudaStream_t cs = nullptr;
+    cudaEvent_t ready = nullptr, done = nullptr;
+    int rank = 0, world = 1;
+};
+
+namespace {
+
+int nccl_fail(ncclResult_t r, const char* what)
+{
+    return dia::fail(DIA_ERR_CUDA, std::string(what) + ": " + ncclGetErrorString(r));
+}
+
+#define DIA_TRY_NCCL(expr)                                  \
+    do {                                                    \
+        ncclResult_t r__ = (expr);                          \
+        if (r__ != ncclSuccess) return nccl_fail(r__, #expr); \
+    } while (0)
+
+/* ranges: recv-left [0,1), send-left [2,3), recv-right [4,5), send-right
+ * [6,7) as global column indices; ext column j holds global column
+ * ext_lo + j, stored rows k*pitch apart. */
+int halo_post(DiaDist* d, float* ext, int64_t ext_lo, int64_t pitch, int K,
+              const int64_t* rg)
+{
+    DIA_TRY_NCCL(ncclGroupStart());
+    for (int k = 0; k < K; ++k) {
+        float* row = ext + (int64_t)k * pitch - ext_lo;
+        const int peer[4] = {d->rank - 1, d->rank - 1, d->rank + 1, d->rank + 1};
+        for (int s = 0; s < 4; ++s) {
+            const int64_t lo = rg[2 * s], hi = rg[2 * s + 1];
+            if (hi <= lo || peer[s] < 0 || peer[s] >= d->world) continue;
+            if (s % 2 == 0)
+                DIA_TRY_NCCL(ncclRecv(row + lo, (size_t)(hi - lo), ncclFloat, peer[s], d->comm,
+                                      d->cs));
+            else
+                DIA_TRY_NCCL(ncclSend(row + lo, (size_t)(hi - lo), ncclFloat, peer[s], d->comm,
+                                      d->cs));
+        }
+    }
+    DIA_TRY_NCCL(ncclGroupEnd());
+    return DIA_OK;
+}
+
+}  // namespace
+
+using namespace dia;
+
+extern "C" int dia_nccl_unique_id(void* out, int nbytes)
+{
+    if (!out || nbytes < (int)sizeof(ncclUniqueId))
+        return fail(DIA_ERR_INVALID, "dia_nccl_unique_id: buffer smaller than ncclUniqueId");
+    ncclUniqueId id;
+    DIA_TRY_NCCL(ncclGetUniqueId(&id));
+    std::memcpy(out, &id, sizeof(id));
+    return DIA_OK;
+}
+
+extern "C" int dia_dist_create(int rank, int world, const void* id, DiaDist** out)
+{
+    if (!out || !id || world < 1 || rank < 0 || rank >= world)
+        return fail(DIA_ERR_INVALID, "dia_dist_create: bad rank/world or null pointer");
+    *out = nullptr;
+    auto* d = new DiaDist();
+    d->rank = rank;
+    d->world = world;
+    ncclUniqueId uid;
+    std::memcpy(&uid, id, sizeof(uid));
+    ncclResult_t r = ncclCommInitRank(&d->comm, world, uid, rank);
+    if (r != ncclSuccess) {
+        delete d;
+        return nccl_fail(r, "ncclCommInitRank");
+    }
+    /* the halo stream gets the highest priority: its small kernels (NCCL's,
+     * the boundary strips) are then dispatched ahead of the interior
+     * kernel's pending CTAs instead of after them */
+    int lo_prio = 0, hi_prio = 0;
+    cudaDeviceGetStreamPriorityRange(&lo_prio, &hi_prio);
+    cudaError_t e = cudaStreamCreateWithPriority(&d->cs, cudaStreamNonBlocking, hi_prio);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&d->ready, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&d->done, cudaEventDisableTiming);
+    if (e != cudaSuccess) {
+        ncclCommDestroy(d->comm);
+        delete d;
+        return cuda_fail(e, "dia_dist_create stream/events");
+    }
+    *out = d;
+    return DIA_OK;
+}
+
+extern "C" int dia_dist_halo_start(DiaDist* d, float* d_ext, int64_t ext_lo, int64_t pitch, int K,
+                                   const int64_t* h_ranges, cudaStream_t stream)
+{
+    if (!d || !d_ext || !h_ranges || K < 0)
+        return fail(DIA_ERR_INVALID, "dia_dist_halo_start: null pointer or bad K");
+    DIA_TRY_CUDA(cudaEventRecord(d->ready, stream));
+    DIA_TRY_CUDA(cudaStreamWaitEvent(d->cs, d->ready, 0));
+    const int rc = halo_post(d, d_ext, ext_lo, pitch, K, h_ranges);
+    if (rc) return rc;
+    DIA_TRY_CUDA(cudaEventRecord(d->done, d->cs));
+    return DIA_OK;
+}
+
+extern "C" int dia_dist_halo_wait(DiaDist* d, cudaStream_t stream)
+{
+    if (!d) return fail(DIA_ERR_INVALID, "dia_dist_halo_wait: null handle");
+    DIA_TRY_CUDA(cudaStreamWaitEvent(stream, d->done, 0));
+    return DIA_OK;
+}
+
+extern "C" int dia_dist_spmv_step(DiaDist* d, int64_t n_rows, int64_t n_cols, int K,
+                                  const int* d_offsets, const float* d_vals, int64_t stride,
+                                  int64_t vrow0, float* d_x_ext, int64_t x_lo, int64_t x_hi,
+                                  float* d_y, const int64_t* h_ranges, int64_t r0, int64_t r1,
+                                  int64_t int_lo, int64_t int_hi, int overlap,
+                                  cudaStream_t stream)
+{
+    if (!d) return fail(DIA_ERR_INVALID, "dia_dist_spmv_step: null handle");
+    int rc = DIA_OK;
+    if (!overlap) {
+        /* exchange first, then one launch over the whole block: the halo is
+         * a few hundred KB (tens of microseconds over NVLink), while two
+         * extra boundary launches cost their tail latency each */
+        if (d->world > 1) {
+            rc = dia_dist_halo_start(d, d_x_ext, x_lo, 0, 1, h_ranges, stream);
+            if (rc == DIA_OK) rc = dia_dist_halo_wait(d, stream);
+            if (rc) return rc;
+        }
+        return dia_spmv_rows(n_rows, n_cols, K, d_offsets, d_vals, stride, vrow0, r0, r1, d_x_ext,
+                             x_lo, x_hi, d_y, stream);
+    }
+    if (overlap == 2 && d->world > 1) {
+        /* the boundary strips run on the halo stream right after the
+         * receive, concurrently with the interior rows on `stream`; `stream`
+         * then waits for them (they write disjoint rows of y) */
+        DIA_TRY_CUDA(cudaEventRecord(d->ready, stream));
+        DIA_TRY_CUDA(cudaStreamWaitEvent(d->cs, d->ready, 0));
+        rc = halo_post(d, d_x_ext, x_lo, 0, 1, h_ranges);
+        if (rc == DIA_OK && int_lo > r0)
+            rc = dia_spmv_rows(n_rows, n_cols, K, d_offsets, d_vals, stride, vrow0, r0, int_lo,
+                               d_x_ext, x_lo, x_hi, d_y, d->cs);
+        if (rc == DIA_OK && r1 > int_hi)
+            rc = dia_spmv_rows(n_rows, n_cols, K, d_offsets, d_vals, stride, vrow0, int_hi, r1,
+                               d_x_ext, x_lo, x_hi, d_y, d->cs);
+        if (rc) return rc;
+        DIA_TRY_CUDA(cudaEventRecord(d->done, d->cs));
+        if (int_hi > int_lo)
+            rc = dia_spmv_rows(n_rows, n_cols, K, d_offsets, d_vals, stride, vrow0, int_lo,
+                               int_hi, d_x_ext, x_lo, x_hi, d_y, stream);
+        if (rc) return rc;
+        return dia_dist_halo_wait(d, stream);
+    }
+    if (d->world > 1) {
+        rc = dia_dist_halo_start(d, d_x_ext, x_lo, 0, 1, h_ranges, stream);
+        if (rc) return rc;
+    }
+    if (int_hi > int_lo)
+        rc = dia_spmv_rows(n_rows, n_cols, K, d_offsets, d_vals, stride, vrow0, int_lo, int_hi,
+                           d_x_ext, x_lo, x_hi, d_y, stream);
+    if (rc) return rc;
+    if (d->world > 1) {
+        rc = dia_dist_halo_wait(d, stream);
+        if (rc) return rc;
+    }
+    if (int_lo > r0)
+        rc = dia_spmv_rows(n_rows, n_cols, K, d_offsets, d_vals, stride, vrow0, r0, int_lo,
+                           d_x_ext, x_lo, x_hi, d_y, stream);
+    if (rc == DIA_OK && r1 > int_hi)
+        rc = dia_spmv_rows(n_rows, n_cols, K, d_offsets, d_vals, stride, vrow0, int_hi, r1,
+                           d_x_ext, x_lo, x_hi, d_y, stream);
+    return rc;
+}
+
+extern "C" int dia_dist_async_error(DiaDist* d)
+{
+    if (!d) return fail(DIA_ERR_INVALID, "dia_dist_async_error: null handle");
+    ncclResult_t ar = ncclSuccess;
+    DIA_TRY_NCCL(ncclCommGetAsyncError(d->comm, &ar));
+    if (ar != ncclSuccess && ar != ncclInProgress) return nccl_fail(ar, "NCCL async error");
+    return DIA_OK;
+}
+
+extern "C" int dia_dist_destroy(DiaDist* d)
+{
+    if (!d) return DIA_OK;
+    if (d->cs) cudaStreamSynchronize(d->cs);
+    if (d->comm) ncclCommDestroy(d->comm);
+    if (d->ready) cudaEventDestroy(d->ready);
+    if (d->done) cudaEventDestroy(d->done);
+    if (d->cs) cudaStreamDestroy(d->cs);
+    delete d;
+    return DIA_OK;
+}

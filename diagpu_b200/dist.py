@@ -71,6 +71,18 @@ class Halo:
         a, b = self.interior()
         return [(lo, hi) for lo, hi in ((self.r0, a), (b, self.r1)) if hi > lo]
 
+    def ranges(self):
+        """Global column ranges [recv-left, send-left, recv-right, send-right]
+        as 8 int64 (the exchange start() posts; empty where no neighbour)."""
+        r = [0] * 8
+        if self.left is not None:
+            lxlo, lxhi = halo_window(self.n, *self.left, self.lo_off, self.hi_off)
+            r[0:4] = [self.xlo, self.r0, self.r0, max(self.r0, lxhi)]
+        if self.right is not None:
+            rxlo, rxhi = halo_window(self.n, *self.right, self.lo_off, self.hi_off)
+            r[4:8] = [self.r1, self.xhi, min(rxlo, self.r1), self.r1]
+        return np.array(r, np.int64)
+
     def start(self, ext: torch.Tensor, group=None):
         """Post the halo sends/receives on ext (column j = global xlo + j);
         returns a handle whose wait() completes the exchange."""
@@ -108,6 +120,15 @@ class Halo:
         return _Pending(works, post)
 
 
+class _NativeWait:
+    def __init__(self, comm):
+        self.comm = comm
+
+    def wait(self):
+        from . import _stream, check, lib
+        check(lib().dia_dist_halo_wait(self.comm.handle, _stream()))
+
+
 class _Pending:
     def __init__(self, works, post):
         self.works, self.post = works, post
@@ -119,20 +140,69 @@ class _Pending:
             v.copy_(buf)
 
 
+class NativeComm:
+    """The library's own NCCL communicator and halo stream (dia_dist_*),
+    created collectively from a unique id broadcast over torch.distributed.
+    Used by DistSpmv / DistSpmspm when the process group runs NCCL."""
+
+    def __init__(self, group=None):
+        import ctypes as C
+        from . import check, lib
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        idbuf = bytearray(128)
+        if rank == 0:
+            cbuf = (C.c_char * 128)()
+            check(lib().dia_nccl_unique_id(cbuf, 128))
+            idbuf = bytearray(cbuf.raw)
+        obj = [bytes(idbuf)]
+        dist.broadcast_object_list(obj, src=0, group=group)
+        raw = (C.c_char * 128).from_buffer_copy(obj[0])
+        self._h = C.c_void_p()
+        check(lib().dia_dist_create(rank, world, raw, C.byref(self._h)))
+        self.rank, self.world = rank, world
+
+    @property
+    def handle(self):
+        return self._h
+
+    def check(self):
+        from . import check, lib
+        check(lib().dia_dist_async_error(self._h))
+
+    def __del__(self):
+        from . import _lib
+        if getattr(self, "_h", None) and self._h.value and _lib is not None:
+            _lib.dia_dist_destroy(self._h)
+            self._h = None
+
+
+def use_native(group=None):
+    return dist.is_initialized() and dist.get_backend(group) == "nccl"
+
+
 # ----------------------------------------------------------------- products
 
 class DistSpmv:
     """y = A*x with A row-partitioned over the process group.
 
     Each rank holds its row block of A (padded rows layout) and an extended
-    x buffer over its halo window; `step()` exchanges the halo, runs the
-    interior rows concurrently with the transfer, then the boundary rows."""
+    x buffer over its halo window.  With NCCL, `step()` is one library call
+    (dia_dist_spmv_step).  Default overlap=2: halo and boundary strips on the
+    library's high-priority stream, concurrently with the interior rows
+    (fastest measured); 1: boundary strips after the interior on one
+    stream; 0: exchange, then one launch over the block.  Without
+    NCCL (gloo/CPU groups) the exchange goes through torch.distributed."""
 
-    def __init__(self, A: DiaRows, halo: Halo, group=None):
+    def __init__(self, A: DiaRows, halo: Halo, group=None, native=None, overlap=2):
         self.A, self.halo, self.group = A, halo, group
         dev = A.vals.device
         self.x_ext = torch.zeros(halo.width, dtype=torch.float32, device=dev)
         self.y = torch.zeros(A.stride, dtype=torch.float32, device=dev)
+        if native is None and halo.world > 1 and use_native(group):
+            native = NativeComm(group)
+        self.native = native
+        self.overlap = overlap
+        self._ranges = halo.ranges()
 
     @property
     def x_own(self):
@@ -141,6 +211,8 @@ class DistSpmv:
 
     def step(self, launches: list | None = None):
         h = self.halo
+        if self.native is not None:
+            return self._native_step(launches)
         pend = h.start(self.x_ext, self.group) if h.world > 1 else None
         a, b = h.interior()
         if b > a:
@@ -153,6 +225,24 @@ class DistSpmv:
             spmv(self.A, self.x_ext, self.y, x_lo=h.xlo, row_lo=lo, row_hi=hi)
             if launches is not None:
                 launches.append("spmv")
+        return self.y
+
+
+    def _native_step(self, launches):
+        import ctypes as C
+        from . import _dptr, _stream, check, lib
+        h, A = self.halo, self.A
+        a, b = h.interior()
+        check(lib().dia_dist_spmv_step(self.native.handle, A.n_rows, A.n_cols, A.K,
+                                       _dptr(A.d_offsets), _dptr(A.vals), A.stride, A.vrow0,
+                                       _dptr(self.x_ext), h.xlo, h.xhi, _dptr(self.y),
+                                       self._ranges.ctypes.data_as(C.c_void_p), h.r0, h.r1,
+                                       a, b, int(self.overlap), _stream()))
+        if launches is not None:
+            launches += (["spmv"] * (int(b > a) + int(a > h.r0) + int(h.r1 > b))
+                         if self.overlap else ["spmv"])
+        if self.overlap == 2 and h.world > 1:
+            pass  # the boundary strips ran on the library's halo stream
         return self.y
 
 
@@ -169,10 +259,21 @@ class DistSpmspm:
         self.plan_all = SpmspmPlan(A, B_ext, b_lo=h.xlo, b_hi=h.xhi)
         self.C = self.plan_all.new_C()
         self.sym = spmspm_symbolic(A.n_rows, A.offsets, B_ext.offsets)
+        self.native = NativeComm(group) if halo.world > 1 and use_native(group) else None
+        self._ranges = halo.ranges()
 
     def step(self, launches: list | None = None):
         h = self.halo
-        pend = h.start(self.B.vals, self.group) if h.world > 1 else None
+        if self.native is not None:
+            import ctypes as C
+            from . import _dptr, _stream, check, lib
+            B = self.B
+            check(lib().dia_dist_halo_start(self.native.handle, _dptr(B.vals), B.vrow0, B.stride,
+                                            B.K, self._ranges.ctypes.data_as(C.c_void_p),
+                                            _stream()))
+            pend = _NativeWait(self.native)
+        else:
+            pend = h.start(self.B.vals, self.group) if h.world > 1 else None
         a, b = h.interior()
         plan_in = self.plan_all if pend is None else self.plan_own
         if b > a:

@@ -193,6 +193,42 @@ int dia_gemm_diag_ex(const float* d_DA, const float* d_DB, const int* d_off_A,
                      const int* d_k_to_idx, int beta, int mode,
                      cudaStream_t stream);
 
+/* ------------------------------------------------- row-partitioned (NCCL) */
+
+/* Native halo exchange for row-block partitioned products over 1..N GPUs,
+ * one process per GPU.  No counterpart in the reference (single-GPU only);
+ * this is the partitioned form of its products.  dia_nccl_unique_id fills
+ * an ncclUniqueId (128 bytes) on one rank; the caller distributes it; every
+ * rank then calls dia_dist_create (collective, blocking), which creates the
+ * NCCL communicator and a private stream. */
+typedef struct DiaDist DiaDist;
+int dia_nccl_unique_id(void* h_id, int nbytes);
+int dia_dist_create(int rank, int world, const void* h_id, DiaDist** dist);
+/* Exchange halo columns of a [K rows x pitch] buffer whose column j holds
+ * global column ext_lo + j.  h_ranges (8 x int64, global columns): receive
+ * from rank-1 [0,1), send to rank-1 [2,3), receive from rank+1 [4,5), send
+ * to rank+1 [6,7); empty ranges are skipped.  halo_start orders the
+ * exchange after the work already on `stream`; halo_wait makes `stream`
+ * wait for it. */
+int dia_dist_halo_start(DiaDist* dist, float* d_ext, int64_t ext_lo, int64_t pitch, int K,
+                        const int64_t* h_ranges, cudaStream_t stream);
+int dia_dist_halo_wait(DiaDist* dist, cudaStream_t stream);
+/* One partitioned SpMV step with a single host call (arguments as
+ * dia_spmv_rows).  overlap == 2 (fastest measured): the halo is received on
+ * the library's high-priority stream, the boundary rows [r0, int_lo) and
+ * [int_hi, r1) run there right after it while the interior rows
+ * [int_lo, int_hi) run on `stream`; `stream` then waits for both.
+ * overlap == 1: interior during the transfer, boundary strips after it, all
+ * on `stream`.  overlap == 0: exchange, then one launch over [r0, r1). */
+int dia_dist_spmv_step(DiaDist* dist, int64_t n_rows, int64_t n_cols, int num_diags,
+                       const int* d_offsets, const float* d_vals, int64_t stride,
+                       int64_t vrow0, float* d_x_ext, int64_t x_lo, int64_t x_hi, float* d_y,
+                       const int64_t* h_ranges, int64_t r0, int64_t r1, int64_t int_lo,
+                       int64_t int_hi, int overlap, cudaStream_t stream);
+/* NCCL's asynchronous error state of the communicator (DIA_OK if none). */
+int dia_dist_async_error(DiaDist* dist);
+int dia_dist_destroy(DiaDist* dist);
+
 /* Device status word shared by the library's kernels.  Kernels that wait on
  * the hardware (the tcgen05 dense-band kernel's mbarrier waits) never spin
  * without bound: on giving up they set a bit here and return early.  Reads
