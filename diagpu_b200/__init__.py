@@ -115,7 +115,13 @@ def _dptr(t, dtype=None):
 
 
 def round_stride(rows: int) -> int:
-    return (rows + ALIGN - 1) // ALIGN * ALIGN
+    """Diagonal stride in floats: rows rounded up to 32 (128-byte rows).
+    When that is a multiple of 2048 floats, 64 floats are added: diagonals a
+    large power of two apart keep the same low address bits, so the many
+    diagonal streams of a product land on the same HBM channels (measured
+    on config 5 C = A*A: 24-27 ms unpadded, 21-22 ms padded)."""
+    s = (rows + ALIGN - 1) // ALIGN * ALIGN
+    return s + 64 if s % 2048 == 0 else s
 
 
 # ------------------------------------------------------------------ storage

@@ -11,7 +11,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libdiagpu_b200.so")
-SOURCES = ["status.cu", "spmv.cu", "spmspm.cu", "spmspm_tiled.cu", "symbolic.cu", "gemm_diag.cu",
+SOURCES = ["status.cu", "spmv.cu", "spmspm.cu", "spmspm_tiled.cu", "spmspm_runpair.cu", "symbolic.cu", "gemm_diag.cu",
            "gemm_diag_tc.cu", "synth.cu", "dist.cu"]
 NVCC = os.environ.get("NVCC", "nvcc")
 FLAGS = ["-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo",

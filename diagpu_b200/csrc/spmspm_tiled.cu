@@ -30,6 +30,23 @@
 
 namespace dia {
 
+struct RunBlock;
+struct RunPairDesc;
+struct RunPairPlan {
+    int P = 0, Q = 0, nblk = 0, i_lo = 0, i_hi = 0;
+    RunBlock* d_blks = nullptr;
+    RunPairDesc* d_rps = nullptr;
+};
+bool runpair_plan_build(const int* hA, int nA, const int* hB, int nB, const int* hC, int nC,
+                        long long A_stride, long long B_stride, long long C_stride,
+                        long long vrow0, long long b_vrow0, int b_lo, int b_hi, int rows_lo,
+                        int rows_hi, RunPairPlan* rp);
+void runpair_plan_free(RunPairPlan* rp);
+int runpair_launch(const RunPairPlan* rp, const float* A, const float* B, float* C,
+                   long long A_stride, long long B_stride, long long C_stride, long long tlo,
+                   long long thi, cudaStream_t stream);
+int runpair_tile_rows();
+
 int launch_pair_sum(const float* U, const float* V, float* O, const OutDesc* outs,
                     const Term* terms, int nOut, int row_lo, int row_hi, bool accumulate,
                     cudaStream_t stream, float avg_terms = -1.0f);
@@ -130,6 +147,7 @@ struct DiaSpmspmPlan {
     OutDesc* d_gouts = nullptr;
     int* d_offs = nullptr;   /* A | B | C offsets on the device */
     float avg_terms = -1.0f; /* pairs per output diagonal */
+    RunPairPlan rp;          /* register-blocked path for run-structured offsets */
 };
 
 namespace {
@@ -137,6 +155,7 @@ namespace {
 int plan_free(DiaSpmspmPlan* p)
 {
     if (!p) return DIA_OK;
+    runpair_plan_free(&p->rp);
     cudaFree(p->d_win);
     cudaFree(p->d_terms);
     cudaFree(p->d_tptr);
@@ -221,8 +240,13 @@ extern "C" int dia_spmspm_plan_create(int64_t n, const int* h_A_off, int nA, con
         if ((rc = cuda(cudaDeviceSynchronize(), "plan build"))) return rc;
     }
 
+    /* run-pair path (stencils, bands): preferred when the offsets allow it */
+    if (nc > 0 && np > 0 && nA > 0)
+        runpair_plan_build(h_A_off, nA, h_B_off, nB, P->C_off.data(), nc, A_stride, B_stride,
+                           C_stride, vrow0, b_vrow0, P->b_lo, P->b_hi, P->rows_lo, P->rows_hi,
+                           &P->rp);
     /* tiled path: interior rows, where every term is in range */
-    if (nc > 0 && np > 0 && nA > 0) {
+    if (nc > 0 && np > 0 && nA > 0 && !P->rp.P) {
         const int dmin = *std::min_element(h_A_off, h_A_off + nA);
         const int dmax = *std::max_element(h_A_off, h_A_off + nA);
         long long lo = std::max<long long>(P->rows_lo, (long long)P->b_lo - dmin + 4);
@@ -325,6 +349,12 @@ extern "C" int dia_spmspm_plan_info(const DiaSpmspmPlan* P, int* n_c, int* h_C_o
         if (h_C_len) h_C_len[c] = P->C_len[c];
         if (h_C_start) h_C_start[c] = P->C_start[c];
     }
+    if (P->rp.P) {
+        if (tile_rows) *tile_rows = -runpair_tile_rows();   /* negative: run-pair kernel */
+        if (tiled_lo) *tiled_lo = P->rp.i_lo;
+        if (tiled_hi) *tiled_hi = P->rp.i_hi;
+        return DIA_OK;
+    }
     if (tile_rows) *tile_rows = P->T;
     if (tiled_lo) *tiled_lo = P->T ? P->i_lo : 0;
     if (tiled_hi) *tiled_hi = P->T ? P->i_hi : 0;
@@ -342,7 +372,18 @@ extern "C" int dia_spmspm_plan_execute(const DiaSpmspmPlan* P, const float* d_A_
     if (!d_A_vals || !d_B_vals || !d_C_vals)
         return fail(DIA_ERR_INVALID, "dia_spmspm_plan_execute: null pointer");
     long long tlo = row_hi, thi = row_hi;
-    if (use_tiles && P->T) {
+    if (use_tiles && P->rp.P) {
+        const long long T = runpair_tile_rows();
+        const long long first = std::max<long long>(0, (row_lo - P->rp.i_lo + T - 1) / T);
+        const long long last = (std::min<long long>(row_hi, P->rp.i_hi) - P->rp.i_lo) / T;
+        if (last > first && row_lo < P->rp.i_hi) {
+            tlo = P->rp.i_lo + first * T;
+            thi = P->rp.i_lo + last * T;
+            const int rc0 = runpair_launch(&P->rp, d_A_vals, d_B_vals, d_C_vals, P->A_stride,
+                                           P->B_stride, P->C_stride, tlo, thi, stream);
+            if (rc0) return rc0;
+        }
+    } else if (use_tiles && P->T) {
         /* whole tiles inside both the interior and [row_lo, row_hi) */
         const long long first = std::max<long long>(0, (row_lo - P->i_lo + P->T - 1) / P->T);
         const long long last = (std::min<long long>(row_hi, P->i_hi) - P->i_lo) / P->T;

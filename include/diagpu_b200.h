@@ -150,8 +150,10 @@ int dia_spmspm_plan_create(int64_t n, const int* h_A_off, int nA, const int* h_B
                            int nB, int64_t A_stride, int64_t B_stride, int64_t C_stride,
                            int64_t vrow0, int64_t nrows, int64_t b_vrow0, int64_t b_lo,
                            int64_t b_hi, DiaSpmspmPlan** plan);
-/* Output structure (any pointer may be NULL), tile rows of the tiled path
- * (0: not used) and the row range it covers. */
+/* Output structure (any pointer may be NULL), the interior kernel's tile
+ * rows (0: generic kernel only; > 0: shared-memory-tiled kernel; < 0: the
+ * register-blocked run-pair kernel, for offsets made of equal-length runs
+ * of consecutive values) and the row range it covers. */
 int dia_spmspm_plan_info(const DiaSpmspmPlan* plan, int* n_c, int* h_C_off, int* h_C_len,
                          int64_t* h_C_start, int* tile_rows, int64_t* tiled_lo,
                          int64_t* tiled_hi);

@@ -174,7 +174,7 @@ def _window_oracle(n, offs, W, wlo, lo, hi, C_off):
     return out
 
 
-@pytest.mark.parametrize("case", ["stencil7", "stencil27", "band", "scatter", "tiny"])
+@pytest.mark.parametrize("case", ["stencil7", "stencil27", "runs2", "band", "scatter", "tiny"])
 def test_tiled_plan_equals_generic(case):
     """The shared-memory-tiled path, the planned generic path and the
     unplanned entry point give identical results (and the tiled kernel is
@@ -185,6 +185,8 @@ def test_tiled_plan_equals_generic(case):
         n = 64 * 64 * 64
         offs = np.array([i + 64 * j + 4096 * k for k in (-1, 0, 1) for j in (-1, 0, 1)
                          for i in (-1, 0, 1)], np.int32)
+    elif case == "runs2":     # runs of two, asymmetric, odd n
+        n, offs = 200_001, np.array([-3001, -3000, -8, -7, 40, 41, 9000, 9001], np.int32)
     elif case == "band":
         n, offs = 100_003, np.arange(-9, 10, dtype=np.int32)
     elif case == "scatter":
@@ -192,10 +194,13 @@ def test_tiled_plan_equals_generic(case):
     else:
         n, offs = 300, np.array([-2, 0, 1], np.int32)
     A = dg.DiaRows.synth(n, n, offs, seed=71)
-    B = dg.DiaRows.synth(n, n, offs[::-1].copy(), seed=72)
+    boffs = offs if case in ("stencil27", "runs2") else offs[::-1].copy()
+    B = dg.DiaRows.synth(n, n, boffs, seed=72)
     plan = dg.SpmspmPlan(A, B)
-    if case in ("stencil7", "band"):
+    if case in ("stencil7", "band"):       # shared-memory-tiled kernel
         assert plan.tile_rows > 0 and plan.tiled[1] > plan.tiled[0]
+    if case in ("stencil27", "runs2"):     # register-blocked run-pair kernel
+        assert plan.tile_rows < 0 and plan.tiled[1] > plan.tiled[0]
     Ct = plan.execute(A, B, plan.new_C())
     Cg = plan.execute(A, B, plan.new_C(), use_tiles=False)
     Cu = dg.spmspm(A, B, method="generic")
