@@ -133,9 +133,14 @@ class _Pending:
     def __init__(self, works, post):
         self.works, self.post = works, post
 
-    def wait(self):
+    def wait(self, timeout=None):
+        """Complete the exchange; with `timeout` (a datetime.timedelta) a
+        neighbour that never posts its side raises instead of blocking."""
         for w in self.works:
-            w.wait()
+            if timeout is None:
+                w.wait()
+            else:
+                w.wait(timeout)
         for v, buf in self.post:
             v.copy_(buf)
 

@@ -93,3 +93,33 @@ def test_halo_plan_partition():
     assert parts[0][0] == 0 and parts[-1][1] == 67108864
     assert all(parts[i][1] == parts[i + 1][0] for i in range(7))
     assert all((p[1] - p[0]) % 32 == 0 for p in parts[:-1])
+
+
+def test_validation_returns_status_not_exit():
+    """Invalid calls return DIA_ERR_* with a message; nothing reaches the
+    GPU (these run without one)."""
+    L = dg.lib()
+    p = C.c_void_p
+    # rows outside the stored block
+    rc = L.dia_spmv_rows(100, 100, 1, p(8), p(8), 32, 0, 0, 100, p(8), 0, 100, p(8), None)
+    assert rc == dg.DIA_ERR_INVALID and "outside the stored block" in L.dia_last_error().decode()
+    # rows x cols beyond int32
+    rc = L.dia_spmv_rows(1 << 31, 10, 1, p(8), p(8), 1 << 32, 0, 0, 10, p(8), 0, 10, p(8), None)
+    assert rc in (dg.DIA_ERR_UNSUPPORTED, dg.DIA_ERR_INVALID)
+    # SpMSpM over the rows layout: B rows outside its buffer
+    rc = L.dia_spmspm_rows(100, p(8), 128, p(8), 1, p(8), 128, 0, -5, 100, p(8), 1, p(8), 128,
+                           p(8), 1, 0, 0, 100, None)
+    assert rc == dg.DIA_ERR_INVALID
+    # planned product: geometry outside the buffers is rejected before any allocation
+    plan = C.c_void_p()
+    one = np.array([0], np.int32)
+    ptr = one.ctypes.data_as(C.c_void_p)
+    rc = L.dia_spmspm_plan_create(100, ptr, 1, ptr, 1, 32, 128, 128, 0, 100, 0, 0, 100,
+                                  C.byref(plan))
+    assert rc == dg.DIA_ERR_INVALID and not plan.value
+    # null handles
+    assert L.dia_spmspm_plan_execute(None, None, None, None, 0, 1, 1, None) == dg.DIA_ERR_INVALID
+    assert L.dia_dist_spmv_step(None, 1, 1, 1, None, None, 32, 0, None, 0, 1, None, None, 0, 1,
+                                0, 1, 0, None) == dg.DIA_ERR_INVALID
+    assert L.dia_dist_create(0, 0, None, C.byref(C.c_void_p())) == dg.DIA_ERR_INVALID
+    assert L.dia_device_status(None, 0) == dg.DIA_ERR_INVALID

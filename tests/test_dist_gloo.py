@@ -64,3 +64,39 @@ def test_row_blocks_cover():
     for n, w in ((67108864, 8), (1000, 3), (33, 2)):
         blocks = [row_block(n, w, r) for r in range(w)]
         assert blocks[0][0] == 0 and blocks[-1][1] == n
+
+
+def _leaver(rank, world, port, q):
+    """Rank 1 leaves between steps, before the halo exchange; rank 0 must
+    get an error from its exchange within the process-group timeout, not
+    hang."""
+    import datetime
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=4))
+    h = Halo(1000, world, rank, -30, 30)
+    ext = torch.zeros(h.width)
+    if rank == 1:
+        os._exit(7)   # leaves between steps; reported through the exit code
+    try:
+        h.start(ext).wait(timeout=datetime.timedelta(seconds=4))
+        q.put((rank, "no error"))
+    except Exception as e:  # noqa: BLE001 - any distributed error is the expected outcome
+        q.put((rank, "error: " + type(e).__name__))
+
+
+def test_missing_peer_is_reported_not_hung():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_leaver, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    rank, res = q.get(timeout=120)
+    for p in ps:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert rank == 0 and res.startswith("error"), res
+    assert ps[1].exitcode == 7
