@@ -92,10 +92,13 @@ def test_config4_dense_band(mode):
 
 @pytest.mark.parametrize("n,lo_a,P,lo_b,Q", [(256, -4, 9, -4, 9), (1000, -64, 129, -64, 129),
                                             (777, -3, 5, 2, 40), (130, 0, 1, 0, 1),
-                                            (5000, -20, 41, -100, 120)])
+                                            (5000, -20, 41, -100, 120),
+                                            (2048, -20, 40, -15, 30),
+                                            (3000, -10, 60, -70, 145)])
 def test_tcgen05_small_bands(n, lo_a, P, lo_b, Q):
     """Tensor-core mode on contiguous bands: ragged last tile, asymmetric
-    and one-diagonal bands, the widest supported B band."""
+    and one-diagonal bands, the widest supported B band, tiles whose
+    accumulator splits into two unequal or B-limited column halves."""
     offA = np.arange(lo_a, lo_a + P, dtype=np.int32)
     offB = np.arange(lo_b, lo_b + Q, dtype=np.int32)
     DA = dg.DiaRows.synth(n, n, offA, seed=11).vals[:, :n].contiguous()
