@@ -22,6 +22,7 @@
  *     plan also precomputes, so execution needs no scratch allocation.
  */
 #include <algorithm>
+#include <climits>
 #include <map>
 #include <vector>
 
@@ -253,85 +254,93 @@ extern "C" int dia_spmspm_plan_create(int64_t n, const int* h_A_off, int nA, con
         long long hi = std::min<long long>(P->rows_hi, (long long)P->b_hi - dmax - 4);
         lo = std::max<long long>(lo, 0);
         lo += mod4(vrow0 - lo);                    /* A slot loads 16-byte aligned */
-        /* clusters of A offsets */
-        std::vector<int> ds(h_A_off, h_A_off + nA);
-        std::sort(ds.begin(), ds.end());
-        std::map<int, int> clus;                   /* offset -> cluster id */
-        std::vector<int> cl_lo, cl_hi;
-        for (int d : ds) {
-            if (cl_lo.empty() || d - cl_lo.back() > kClusterSpan) {
-                cl_lo.push_back(d);
-                cl_hi.push_back(d);
-            }
-            cl_hi.back() = d;
-            clus[d] = (int)cl_lo.size() - 1;
-        }
         int dev = 0, smem_max = 0;
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-        /* only tiles of >= 128 rows: with fewer rows per lane the per-term
-         * overhead outweighs the shared-memory reuse (measured: a 27-point
-         * stencil product ran slower at 64-row tiles than the generic
-         * kernel) */
-        for (int R : {8, 4}) {
-            const int T = 32 * R;
-            if (hi - lo < 2LL * T) continue;
-            std::map<std::pair<int, int>, int> wid;
-            std::vector<Window> win;
-            std::vector<int2> terms;
-            std::vector<int> tptr(nc + 1);
-            int soff = nA * T;
-            const long long align = mod4(b_vrow0 - lo);   /* start row offset alignment */
-            std::vector<int> wstart;
-            for (int c = 0; c < nc; ++c) {
-                tptr[c] = (int)terms.size();
-                for (int q = ptr[c]; q < ptr[c + 1]; ++q) {
-                    const int a = pa[q], b = pb[q], da = h_A_off[a];
-                    const int cl = clus[da];
-                    auto key = std::make_pair(b, cl);
-                    auto it = wid.find(key);
-                    int w;
-                    if (it == wid.end()) {
-                        const long long s = cl_lo[cl] - mod4(cl_lo[cl] - align);
-                        const long long len = (cl_hi[cl] + T - s + 3) / 4 * 4;
-                        Window W;
-                        W.src = (long long)b * B_stride - b_vrow0 + s;
-                        W.soff = soff;
-                        W.len4 = (int)(len / 4);
-                        soff += (int)len;
-                        w = (int)win.size();
-                        win.push_back(W);
-                        wstart.push_back((int)s);
-                        wid[key] = w;
-                    } else {
-                        w = it->second;
-                    }
-                    terms.push_back(make_int2(a * T, win[w].soff + (da - wstart[w])));
+        /* first try clusters of span <= kClusterSpan at two CTAs per SM; if
+         * that does not fit, one cluster spanning all of A's offsets (one B
+         * window per B diagonal, e.g. 32 scattered offsets in [-512, 512])
+         * at one CTA per SM with up to all of the shared memory */
+        for (int wide = 0; wide < 2 && !P->T; ++wide) {
+            const int span = wide ? INT_MAX : kClusterSpan;
+            const int cap = wide ? smem_max : std::min(smem_max, kTileSmemCap);
+            /* clusters of A offsets */
+            std::vector<int> ds(h_A_off, h_A_off + nA);
+            std::sort(ds.begin(), ds.end());
+            std::map<int, int> clus;                   /* offset -> cluster id */
+            std::vector<int> cl_lo, cl_hi;
+            for (int d : ds) {
+                if (cl_lo.empty() || (long long)d - cl_lo.back() > span) {
+                    cl_lo.push_back(d);
+                    cl_hi.push_back(d);
                 }
+                cl_hi.back() = d;
+                clus[d] = (int)cl_lo.size() - 1;
             }
-            tptr[nc] = (int)terms.size();
-            const int smem = soff * 4 + (int)terms.size() * 8 + (nc + 1) * 4;
-            /* at least two CTAs per SM to overlap one tile's copies with
-             * another's products */
-            if (smem > std::min(smem_max, kTileSmemCap)) continue;
-            P->T = T;
-            P->i_lo = (int)lo;
-            P->i_hi = (int)(lo + (hi - lo) / T * T);
-            P->nwin = (int)win.size();
-            P->nterms = (int)terms.size();
-            P->stage_floats = soff;
-            P->smem = smem;
-            if ((rc = cuda(cudaMalloc(&P->d_win, sizeof(Window) * win.size()), "cudaMalloc")) ||
-                (rc = cuda(cudaMalloc(&P->d_terms, sizeof(int2) * terms.size()), "cudaMalloc")) ||
-                (rc = cuda(cudaMalloc(&P->d_tptr, sizeof(int) * tptr.size()), "cudaMalloc")) ||
-                (rc = cuda(cudaMemcpy(P->d_win, win.data(), sizeof(Window) * win.size(),
-                                      cudaMemcpyHostToDevice), "cudaMemcpy")) ||
-                (rc = cuda(cudaMemcpy(P->d_terms, terms.data(), sizeof(int2) * terms.size(),
-                                      cudaMemcpyHostToDevice), "cudaMemcpy")) ||
-                (rc = cuda(cudaMemcpy(P->d_tptr, tptr.data(), sizeof(int) * tptr.size(),
-                                      cudaMemcpyHostToDevice), "cudaMemcpy")))
-                return rc;
-            break;
+            /* only tiles of >= 128 rows: with fewer rows per lane the per-term
+             * overhead outweighs the shared-memory reuse (measured: a 27-point
+             * stencil product ran slower at 64-row tiles than the generic
+             * kernel) */
+            for (int R : {8, 4}) {
+                const int T = 32 * R;
+                if (hi - lo < 2LL * T) continue;
+                std::map<std::pair<int, int>, int> wid;
+                std::vector<Window> win;
+                std::vector<int2> terms;
+                std::vector<int> tptr(nc + 1);
+                int soff = nA * T;
+                const long long align = mod4(b_vrow0 - lo);   /* start row offset alignment */
+                std::vector<int> wstart;
+                for (int c = 0; c < nc; ++c) {
+                    tptr[c] = (int)terms.size();
+                    for (int q = ptr[c]; q < ptr[c + 1]; ++q) {
+                        const int a = pa[q], b = pb[q], da = h_A_off[a];
+                        const int cl = clus[da];
+                        auto key = std::make_pair(b, cl);
+                        auto it = wid.find(key);
+                        int w;
+                        if (it == wid.end()) {
+                            const long long s = cl_lo[cl] - mod4(cl_lo[cl] - align);
+                            const long long len = (cl_hi[cl] + T - s + 3) / 4 * 4;
+                            Window W;
+                            W.src = (long long)b * B_stride - b_vrow0 + s;
+                            W.soff = soff;
+                            W.len4 = (int)(len / 4);
+                            soff += (int)len;
+                            w = (int)win.size();
+                            win.push_back(W);
+                            wstart.push_back((int)s);
+                            wid[key] = w;
+                        } else {
+                            w = it->second;
+                        }
+                        terms.push_back(make_int2(a * T, win[w].soff + (da - wstart[w])));
+                    }
+                }
+                tptr[nc] = (int)terms.size();
+                const int smem = soff * 4 + (int)terms.size() * 8 + (nc + 1) * 4;
+                /* clustered: at least two CTAs per SM, so one tile's copies
+                 * overlap another's products */
+                if (smem > cap) continue;
+                P->T = T;
+                P->i_lo = (int)lo;
+                P->i_hi = (int)(lo + (hi - lo) / T * T);
+                P->nwin = (int)win.size();
+                P->nterms = (int)terms.size();
+                P->stage_floats = soff;
+                P->smem = smem;
+                if ((rc = cuda(cudaMalloc(&P->d_win, sizeof(Window) * win.size()), "cudaMalloc")) ||
+                    (rc = cuda(cudaMalloc(&P->d_terms, sizeof(int2) * terms.size()), "cudaMalloc")) ||
+                    (rc = cuda(cudaMalloc(&P->d_tptr, sizeof(int) * tptr.size()), "cudaMalloc")) ||
+                    (rc = cuda(cudaMemcpy(P->d_win, win.data(), sizeof(Window) * win.size(),
+                                          cudaMemcpyHostToDevice), "cudaMemcpy")) ||
+                    (rc = cuda(cudaMemcpy(P->d_terms, terms.data(), sizeof(int2) * terms.size(),
+                                          cudaMemcpyHostToDevice), "cudaMemcpy")) ||
+                    (rc = cuda(cudaMemcpy(P->d_tptr, tptr.data(), sizeof(int) * tptr.size(),
+                                          cudaMemcpyHostToDevice), "cudaMemcpy")))
+                    return rc;
+                break;
+            }
         }
     }
     *out = P;

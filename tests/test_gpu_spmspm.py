@@ -197,7 +197,7 @@ def test_tiled_plan_equals_generic(case):
     boffs = offs if case in ("stencil27", "runs2") else offs[::-1].copy()
     B = dg.DiaRows.synth(n, n, boffs, seed=72)
     plan = dg.SpmspmPlan(A, B)
-    if case in ("stencil7", "band"):       # shared-memory-tiled kernel
+    if case in ("stencil7", "band", "scatter"):   # shared-memory-tiled kernel
         assert plan.tile_rows > 0 and plan.tiled[1] > plan.tiled[0]
     if case in ("stencil27", "runs2"):     # register-blocked run-pair kernel
         assert plan.tile_rows < 0 and plan.tiled[1] > plan.tiled[0]
