@@ -54,8 +54,8 @@ int launch_pair_sum(const float* U, const float* V, float* O, const OutDesc* out
 
 constexpr int kClusterSpan = 64;       /* max span of one A-offset cluster */
 constexpr int kTileSmemCap = 100 * 1024;
-constexpr int kTileThreads = 256;
-constexpr int kTileWarps = kTileThreads / 32;
+constexpr int kTileThreads = 256;       /* CTAs that share an SM */
+constexpr int kTileThreadsSolo = 1024;  /* a CTA alone on its SM (wide windows) */
 
 struct Window {
     long long src;   /* element offset in B_vals of the window at tile row 0 */
@@ -80,16 +80,17 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const float* src)
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 
-template <int R>
-__global__ void __launch_bounds__(kTileThreads) tile_sum_kernel(TileArgs p)
+template <int R, int NT>
+__global__ void __launch_bounds__(NT) tile_sum_kernel(TileArgs p)
 {
+    constexpr int kTileWarps = NT / 32;
     extern __shared__ __align__(16) float sm[];
     constexpr int T = 32 * R;
     int2* s_terms = (int2*)(sm + p.stage_floats);
     int* s_tptr = (int*)(s_terms + p.nterms);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    for (int t = tid; t < p.nterms; t += kTileThreads) s_terms[t] = p.terms[t];
-    for (int c = tid; c <= p.nC; c += kTileThreads) s_tptr[c] = p.tptr[c];
+    for (int t = tid; t < p.nterms; t += NT) s_terms[t] = p.terms[t];
+    for (int c = tid; c <= p.nC; c += NT) s_tptr[c] = p.tptr[c];
     const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(sm);
 
     for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x) {
@@ -417,19 +418,38 @@ extern "C" int dia_spmspm_plan_execute(const DiaSpmspmPlan* P, const float* d_A_
             a.ntiles = (int)((thi - tlo) / P->T);
             a.T = P->T;
             a.stage_floats = P->stage_floats;
-            const void* k = P->T == 256 ? (const void*)tile_sum_kernel<8>
-                          : P->T == 128 ? (const void*)tile_sum_kernel<4>
-                          : P->T == 64 ? (const void*)tile_sum_kernel<2>
-                                       : (const void*)tile_sum_kernel<1>;
+            auto pick = [&](bool solo) -> const void* {
+                if (solo)
+                    return P->T == 256 ? (const void*)tile_sum_kernel<8, kTileThreadsSolo>
+                         : P->T == 128 ? (const void*)tile_sum_kernel<4, kTileThreadsSolo>
+                         : P->T == 64 ? (const void*)tile_sum_kernel<2, kTileThreadsSolo>
+                                      : (const void*)tile_sum_kernel<1, kTileThreadsSolo>;
+                return P->T == 256 ? (const void*)tile_sum_kernel<8, kTileThreads>
+                     : P->T == 128 ? (const void*)tile_sum_kernel<4, kTileThreads>
+                     : P->T == 64 ? (const void*)tile_sum_kernel<2, kTileThreads>
+                                  : (const void*)tile_sum_kernel<1, kTileThreads>;
+            };
+            const void* k = pick(false);
             DIA_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               P->smem));
             int per_sm = 0;
             DIA_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kTileThreads,
                                                                        P->smem));
+            /* a CTA that has its SM to itself runs 32 warps: with 8 the
+             * shared-memory latency of the products is exposed (measured on
+             * config 3: 12.5 % warps active, 37 % issue) */
+            int nt = kTileThreads;
+            if (per_sm <= 1) {
+                k = pick(true);
+                nt = kTileThreadsSolo;
+                DIA_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  P->smem));
+                per_sm = 1;
+            }
             const int grid = (int)std::min<long long>(a.ntiles,
                                                       (long long)std::max(per_sm, 1) * num_sms());
             void* args[] = {&a};
-            DIA_TRY_CUDA(cudaLaunchKernel(k, grid, kTileThreads, args, P->smem, stream));
+            DIA_TRY_CUDA(cudaLaunchKernel(k, grid, nt, args, P->smem, stream));
         }
     }
     int rc = DIA_OK;
