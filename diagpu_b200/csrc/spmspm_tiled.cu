@@ -150,6 +150,11 @@ struct DiaSpmspmPlan {
     int* d_offs = nullptr;   /* A | B | C offsets on the device */
     float avg_terms = -1.0f; /* pairs per output diagonal */
     RunPairPlan rp;          /* register-blocked path for run-structured offsets */
+    /* edge rows run on this high-priority stream, concurrently with the
+     * interior kernel on the caller's stream (they write disjoint rows);
+     * executions of one plan that overlap on the host share it */
+    cudaStream_t side = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
 };
 
 namespace {
@@ -164,6 +169,9 @@ int plan_free(DiaSpmspmPlan* p)
     cudaFree(p->d_gterms);
     cudaFree(p->d_gouts);
     cudaFree(p->d_offs);
+    if (p->side) cudaStreamDestroy(p->side);
+    if (p->fork) cudaEventDestroy(p->fork);
+    if (p->join) cudaEventDestroy(p->join);
     delete p;
     return DIA_OK;
 }
@@ -344,6 +352,19 @@ extern "C" int dia_spmspm_plan_create(int64_t n, const int* h_A_off, int nA, con
             }
         }
     }
+    {
+        int lo_prio = 0, hi_prio = 0;
+        cudaDeviceGetStreamPriorityRange(&lo_prio, &hi_prio);
+        if ((rc = cuda(cudaStreamCreateWithPriority(&P->side, cudaStreamNonBlocking, hi_prio),
+                       "cudaStreamCreateWithPriority")) ||
+            (rc = cuda(cudaEventCreateWithFlags(&P->fork, cudaEventDisableTiming),
+                       "cudaEventCreate")) ||
+            (rc = cuda(cudaEventCreateWithFlags(&P->join, cudaEventDisableTiming),
+                       "cudaEventCreate"))) {
+            plan_free(P);
+            return rc;
+        }
+    }
     *out = P;
     return DIA_OK;
 }
@@ -382,6 +403,7 @@ extern "C" int dia_spmspm_plan_execute(const DiaSpmspmPlan* P, const float* d_A_
     if (!d_A_vals || !d_B_vals || !d_C_vals)
         return fail(DIA_ERR_INVALID, "dia_spmspm_plan_execute: null pointer");
     long long tlo = row_hi, thi = row_hi;
+    int kind = 0;   /* interior kernel: 1 run-pair, 2 tiled */
     if (use_tiles && P->rp.P) {
         const long long T = runpair_tile_rows();
         const long long first = std::max<long long>(0, (row_lo - P->rp.i_lo + T - 1) / T);
@@ -389,9 +411,7 @@ extern "C" int dia_spmspm_plan_execute(const DiaSpmspmPlan* P, const float* d_A_
         if (last > first && row_lo < P->rp.i_hi) {
             tlo = P->rp.i_lo + first * T;
             thi = P->rp.i_lo + last * T;
-            const int rc0 = runpair_launch(&P->rp, d_A_vals, d_B_vals, d_C_vals, P->A_stride,
-                                           P->B_stride, P->C_stride, tlo, thi, stream);
-            if (rc0) return rc0;
+            kind = 1;
         }
     } else if (use_tiles && P->T) {
         /* whole tiles inside both the interior and [row_lo, row_hi) */
@@ -400,66 +420,82 @@ extern "C" int dia_spmspm_plan_execute(const DiaSpmspmPlan* P, const float* d_A_
         if (last > first && row_lo < P->i_hi) {
             tlo = P->i_lo + first * P->T;
             thi = P->i_lo + last * P->T;
-            TileArgs a{};
-            a.A = d_A_vals;
-            a.B = d_B_vals;
-            a.C = d_C_vals;
-            a.win = P->d_win;
-            a.terms = P->d_terms;
-            a.tptr = P->d_tptr;
-            a.nA = P->nA;
-            a.nwin = P->nwin;
-            a.nC = P->nC;
-            a.nterms = P->nterms;
-            a.A_stride = P->A_stride;
-            a.C_stride = P->C_stride;
-            a.vrow0 = P->vrow0;
-            a.i_lo = (int)tlo;
-            a.ntiles = (int)((thi - tlo) / P->T);
-            a.T = P->T;
-            a.stage_floats = P->stage_floats;
-            auto pick = [&](bool solo) -> const void* {
-                if (solo)
-                    return P->T == 256 ? (const void*)tile_sum_kernel<8, kTileThreadsSolo>
-                         : P->T == 128 ? (const void*)tile_sum_kernel<4, kTileThreadsSolo>
-                         : P->T == 64 ? (const void*)tile_sum_kernel<2, kTileThreadsSolo>
-                                      : (const void*)tile_sum_kernel<1, kTileThreadsSolo>;
-                return P->T == 256 ? (const void*)tile_sum_kernel<8, kTileThreads>
-                     : P->T == 128 ? (const void*)tile_sum_kernel<4, kTileThreads>
-                     : P->T == 64 ? (const void*)tile_sum_kernel<2, kTileThreads>
-                                  : (const void*)tile_sum_kernel<1, kTileThreads>;
-            };
-            const void* k = pick(false);
-            DIA_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              P->smem));
-            int per_sm = 0;
-            DIA_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kTileThreads,
-                                                                       P->smem));
-            /* a CTA that has its SM to itself runs 32 warps: with 8 the
-             * shared-memory latency of the products is exposed (measured on
-             * config 3: 12.5 % warps active, 37 % issue) */
-            int nt = kTileThreads;
-            if (per_sm <= 1) {
-                k = pick(true);
-                nt = kTileThreadsSolo;
-                DIA_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                  P->smem));
-                per_sm = 1;
-            }
-            const int grid = (int)std::min<long long>(a.ntiles,
-                                                      (long long)std::max(per_sm, 1) * num_sms());
-            void* args[] = {&a};
-            DIA_TRY_CUDA(cudaLaunchKernel(k, grid, nt, args, P->smem, stream));
+            kind = 2;
         }
+    }
+    const bool edges = tlo > row_lo || row_hi > thi;
+    cudaStream_t es = stream;
+    if (edges && kind && P->side) {
+        DIA_TRY_CUDA(cudaEventRecord(P->fork, stream));
+        DIA_TRY_CUDA(cudaStreamWaitEvent(P->side, P->fork, 0));
+        es = P->side;
     }
     int rc = DIA_OK;
     const float* U = d_A_vals;
     if (tlo > row_lo)
         rc = launch_pair_sum(U, d_B_vals, d_C_vals, P->d_gouts, P->d_gterms, P->nC, (int)row_lo,
-                             (int)tlo, false, stream, P->avg_terms);
+                             (int)tlo, false, es, P->avg_terms);
     if (rc == DIA_OK && row_hi > thi)
         rc = launch_pair_sum(U, d_B_vals, d_C_vals, P->d_gouts, P->d_gterms, P->nC, (int)thi,
-                             (int)row_hi, false, stream, P->avg_terms);
+                             (int)row_hi, false, es, P->avg_terms);
+    if (es != stream) DIA_TRY_CUDA(cudaEventRecord(P->join, es));
+    if (rc) return rc;
+    if (kind == 1) {
+        rc = runpair_launch(&P->rp, d_A_vals, d_B_vals, d_C_vals, P->A_stride, P->B_stride,
+                            P->C_stride, tlo, thi, stream);
+    } else if (kind == 2) {
+        TileArgs a{};
+        a.A = d_A_vals;
+        a.B = d_B_vals;
+        a.C = d_C_vals;
+        a.win = P->d_win;
+        a.terms = P->d_terms;
+        a.tptr = P->d_tptr;
+        a.nA = P->nA;
+        a.nwin = P->nwin;
+        a.nC = P->nC;
+        a.nterms = P->nterms;
+        a.A_stride = P->A_stride;
+        a.C_stride = P->C_stride;
+        a.vrow0 = P->vrow0;
+        a.i_lo = (int)tlo;
+        a.ntiles = (int)((thi - tlo) / P->T);
+        a.T = P->T;
+        a.stage_floats = P->stage_floats;
+        auto pick = [&](bool solo) -> const void* {
+            if (solo)
+                return P->T == 256 ? (const void*)tile_sum_kernel<8, kTileThreadsSolo>
+                     : P->T == 128 ? (const void*)tile_sum_kernel<4, kTileThreadsSolo>
+                     : P->T == 64 ? (const void*)tile_sum_kernel<2, kTileThreadsSolo>
+                                  : (const void*)tile_sum_kernel<1, kTileThreadsSolo>;
+            return P->T == 256 ? (const void*)tile_sum_kernel<8, kTileThreads>
+                 : P->T == 128 ? (const void*)tile_sum_kernel<4, kTileThreads>
+                 : P->T == 64 ? (const void*)tile_sum_kernel<2, kTileThreads>
+                              : (const void*)tile_sum_kernel<1, kTileThreads>;
+        };
+        const void* k = pick(false);
+        DIA_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          P->smem));
+        int per_sm = 0;
+        DIA_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kTileThreads,
+                                                                   P->smem));
+        /* a CTA that has its SM to itself runs 32 warps: with 8 the
+         * shared-memory latency of the products is exposed (measured on
+         * config 3: 12.5 % warps active, 37 % issue) */
+        int nt = kTileThreads;
+        if (per_sm <= 1) {
+            k = pick(true);
+            nt = kTileThreadsSolo;
+            DIA_TRY_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              P->smem));
+            per_sm = 1;
+        }
+        const int grid = (int)std::min<long long>(a.ntiles,
+                                                  (long long)std::max(per_sm, 1) * num_sms());
+        void* args[] = {&a};
+        DIA_TRY_CUDA(cudaLaunchKernel(k, grid, nt, args, P->smem, stream));
+    }
+    if (es != stream) DIA_TRY_CUDA(cudaStreamWaitEvent(stream, P->join, 0));
     return rc;
 }
 
