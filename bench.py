@@ -119,13 +119,15 @@ class Clocks:
 
 # ---------------------------------------------------------------- timing
 
-def timed(fn, steps, warmup, *, flush=None, per_launch=False):
+def timed(fn, steps, warmup, *, flush=None, per_launch=False, world=1):
     """Mean ms of fn() over `steps` after `warmup`, CUDA events on the
     current stream; with per_launch each call is bracketed by its own events
-    and preceded by flush() (outside the bracket)."""
+    and preceded by flush() (outside the bracket).  With world > 1 a barrier
+    precedes the timed region, so a step that exchanges halos does not start
+    its clock while the peer rank is still setting up."""
     for _ in range(warmup):
         fn()
-    torch.cuda.synchronize()
+    barrier(world)
     if per_launch:
         tot = 0.0
         for _ in range(steps):
@@ -369,7 +371,7 @@ def run_ours(args):
     B_ext.vals[:, r0 - halo.xlo:r1 - halo.xlo] = A.vals[:, :r1 - r0]
     dm = DistSpmspm(A, B_ext, halo)
     ksp = max(3, min(K, 10))
-    mm_ms = max_over_ranks(timed(lambda: dm.step(), ksp, max(1, min(W, 3))), world)
+    mm_ms = max_over_ranks(timed(lambda: dm.step(), ksp, max(1, min(W, 3)), world=world), world)
     sym = dm.sym
     fl = spmspm_useful(N5, OFF5, OFF5, sym, 0, N5)
     nnzC = int(sym["C_len"].astype(np.int64).sum())
