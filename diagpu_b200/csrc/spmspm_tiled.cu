@@ -88,9 +88,12 @@ __global__ void __launch_bounds__(NT) tile_sum_kernel(TileArgs p)
     constexpr int T = 32 * R;
     int2* s_terms = (int2*)(sm + p.stage_floats);
     int* s_tptr = (int*)(s_terms + p.nterms);
+    /* window table after the term lists, 8-byte aligned */
+    Window* s_win = (Window*)(((uintptr_t)(s_tptr + p.nC + 1) + 7) & ~(uintptr_t)7);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     for (int t = tid; t < p.nterms; t += NT) s_terms[t] = p.terms[t];
     for (int c = tid; c <= p.nC; c += NT) s_tptr[c] = p.tptr[c];
+    for (int w = tid; w < p.nwin; w += NT) s_win[w] = p.win[w];
     const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(sm);
 
     for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x) {
@@ -102,7 +105,7 @@ __global__ void __launch_bounds__(NT) tile_sum_kernel(TileArgs p)
                 cp_async16(sbase + (uint32_t)(a * T + 4 * q) * 4u, src + 4 * q);
         }
         for (int w = warp; w < p.nwin; w += kTileWarps) {
-            const Window wd = p.win[w];
+            const Window wd = s_win[w];
             const float* src = p.B + wd.src + t0;
             for (int q = lane; q < wd.len4; q += 32)
                 cp_async16(sbase + (uint32_t)(wd.soff + 4 * q) * 4u, src + 4 * q);
@@ -327,7 +330,8 @@ extern "C" int dia_spmspm_plan_create(int64_t n, const int* h_A_off, int nA, con
                     }
                 }
                 tptr[nc] = (int)terms.size();
-                const int smem = soff * 4 + (int)terms.size() * 8 + (nc + 1) * 4;
+                const int smem = (soff * 4 + (int)terms.size() * 8 + (nc + 1) * 4 + 7) / 8 * 8 +
+                                 (int)win.size() * (int)sizeof(Window);
                 /* clustered: at least two CTAs per SM, so one tile's copies
                  * overlap another's products */
                 if (smem > cap) continue;
