@@ -269,6 +269,18 @@ def single_gpu_extras(dg, steps, warmup, hbm, src):
                 "metric": "gemm_diag_useful_GFLOPs", "value": round(fl / ms / 1e6, 2),
                 "unit": "GFLOP/s", "ms": round(ms, 4), "bytes": byts, "useful_flops": fl,
                 "roofline": roofline(byts / ms / 1e6, hbm, src), "mode": "auto"})
+    del DA, DB, C
+    # matrix-power chain H^8 of the config-1 operator, symbolic phase on the device
+    fn, byts = _only_chain(dg)
+    ms = timed(fn, max(3, steps // 10), min(warmup, 3))
+    fnh, _ = _only_chain(dg, host=True)
+    ms_host = timed(fnh, 3, 1)
+    out.append({"workload": f"config1 operator power chain H^{CHAIN_K} ({CHAIN_K - 1} products, "
+                            "device-side symbolic phase, no host synchronisation)",
+                "metric": "chain_GBps", "value": round(byts / ms / 1e6, 1), "unit": "GB/s",
+                "ms": round(ms, 4), "bytes": byts,
+                "roofline": roofline(byts / ms / 1e6, hbm, src),
+                "host_planned_ms": round(ms_host, 4)})
     return out
 
 
@@ -514,6 +526,48 @@ def _only_gemm4(dg, n=262144, hb=64, mode=0):
     return fn, 4 * (2 * nnz_rows(n, goff, 0, n) + tot)
 
 
+def _chain_offsets(offs, k):
+    """Offsets of H^k (host sumsets; structure only)."""
+    P = np.asarray(offs, np.int64)
+    for _ in range(k - 1):
+        P = np.unique((P[:, None] + np.asarray(offs, np.int64)[None, :]).ravel())
+    return P
+
+
+def chain_bytes(n, offs, k):
+    """4 * (nnz(P_j) + nnz(H) + nnz(P_{j+1})) summed over the steps j = 1 .. k-1."""
+    tot = 0
+    for j in range(1, k):
+        Pj = _chain_offsets(offs, j)
+        Pj1 = _chain_offsets(offs, j + 1)
+        Pj, Pj1 = Pj[np.abs(Pj) < n], Pj1[np.abs(Pj1) < n]
+        tot += 4 * (nnz_rows(n, Pj, 0, n) + nnz_rows(n, offs, 0, n) + nnz_rows(n, Pj1, 0, n))
+    return tot
+
+
+CHAIN_K = 8
+CHAIN_OFF = np.array([-1024, -1, 0, 1, 1024], np.int32)
+
+
+def _only_chain(dg, host=False, n=1 << 20, k=CHAIN_K):
+    """H^k of the config-1 operator: k-1 products P_{j+1} = P_j * H."""
+    H = dg.DiaRows.synth(n, n, CHAIN_OFF, SEED_A)
+    if host:
+        def fn():
+            P = H
+            for _ in range(k - 1):
+                P = dg.spmspm(P, H)
+            return P
+    else:
+        chain = dg.PowerChain(H, max_diags=len(_chain_offsets(CHAIN_OFF, k)) + 8)
+
+        def fn():
+            chain.reset()
+            for _ in range(k - 1):
+                chain.step()
+    return fn, chain_bytes(n, CHAIN_OFF, k)
+
+
 # name -> builder(dg) returning (callable, algorithmic bytes); the "_s" cases
 # are reduced sizes (<= a few GB on the device) for ncu captures
 ONLY = {
@@ -526,6 +580,8 @@ ONLY = {
                                                                 16384], np.int32)),
     "spmspm3": lambda dg: _only_spmspm(dg, 1_000_000, _scat(301), _scat(302), kind=1),
     "gemm4": lambda dg: _only_gemm4(dg),
+    "chain1": lambda dg: _only_chain(dg),
+    "chain1_host": lambda dg: _only_chain(dg, host=True),
     "gemm4_simt": lambda dg: _only_gemm4(dg, mode=1),
 }
 

@@ -84,6 +84,13 @@ def lib():
         L.dia_device_status.restype = i
         L.dia_synth_rows.argtypes = [u64, i64, i64, i, p, p, i, f, f, i64, i64, i64, p, p]
         L.dia_synth_vector.argtypes = [u64, i64, i64, f, f, p, p]
+        L.dia_spmspm_device_workspace.argtypes = [i64, i, i, i]
+        L.dia_spmspm_device_workspace.restype = i64
+        L.dia_spmspm_symbolic_device.argtypes = [i64, p, p, i, p, i, p, p, i, p, i64, p]
+        L.dia_spmspm_rows_device.argtypes = [i64, p, p, i, p, i64, p, i, p, i64, p, p, i, p,
+                                             i64, p, i64, p]
+        for name in ("dia_spmspm_symbolic_device", "dia_spmspm_rows_device"):
+            getattr(L, name).restype = i
         for name in ("dia_spmv_recon", "dia_spmv_rows", "dia_spmspm_symbolic", "dia_spmspm_hm",
                      "dia_spmspm_hm_noalloc", "dia_spmspm_rows", "dia_gemm_diag", "dia_gemm_diag_ex", "dia_synth_rows",
                      "dia_synth_vector"):
@@ -271,6 +278,90 @@ def spmspm_hm(A_values, A_starts, A_off, A_len, B_values, B_starts, B_len, B_loo
                               _dptr(C_starts, torch.int64), _dptr(C_off, torch.int32),
                               _dptr(C_len, torch.int32), C_off.numel(), n, _stream(stream)))
     return C_values
+
+
+def spmspm_symbolic_device(n, d_A_off, d_nA, nA_cap, d_B_off, nC_cap, *, stream=None):
+    """Output offsets of C = A*B computed on the device (dia_spmspm_symbolic_device).
+
+    d_A_off (int32, capacity nA_cap) and d_nA (int32 [1]) are device
+    tensors, d_B_off the device offsets of B.  Returns device tensors
+    (C_off [nC_cap], nC [1]) without synchronising; nC[0] > nC_cap means the
+    capacity was too small."""
+    dev = d_A_off.device
+    C_off = torch.zeros(max(nC_cap, 1), dtype=torch.int32, device=dev)
+    nC = torch.zeros(1, dtype=torch.int32, device=dev)
+    L = lib()
+    ws = L.dia_spmspm_device_workspace(n, nA_cap, len(d_B_off), nC_cap)
+    if ws < 0:
+        raise DiaError(DIA_ERR_INVALID, "dia_spmspm_device_workspace: bad sizes")
+    work = torch.empty(max(ws, 1), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        check(L.dia_spmspm_symbolic_device(n, _dptr(d_A_off, torch.int32), _dptr(d_nA, torch.int32),
+                                           nA_cap, _dptr(d_B_off, torch.int32), len(d_B_off),
+                                           _dptr(C_off), _dptr(nC), nC_cap, _dptr(work), ws,
+                                           _stream(stream)))
+    return C_off, nC
+
+
+class PowerChain:
+    """Matrix-power chain P_{k+1} = P_k * H entirely on the device.
+
+    H is a whole matrix (vrow0 = 0) with few diagonals.  Each step() runs
+    dia_spmspm_rows_device: the output offsets (sumset) and the pair lists
+    are built on the GPU, so no step synchronises with the host.  P_k lives
+    in one of two ping-pong buffers of max_diags diagonals; power() returns
+    the current P_k (it reads the diagonal count, one synchronisation, and
+    the returned matrix shares the buffer the step after next overwrites).
+    Results equal repeated spmspm(P, H) bit for bit."""
+
+    def __init__(self, H: DiaRows, max_diags: int, *, stream=None):
+        if H.vrow0 != 0 or H.nrows != H.n_rows or H.n_rows != H.n_cols:
+            raise DiaError(DIA_ERR_INVALID, "PowerChain: H must be a whole square matrix")
+        self.H, self.n, self.cap = H, H.n_rows, int(max_diags)
+        if self.cap < H.K:
+            raise DiaError(DIA_ERR_INVALID, "PowerChain: max_diags below H's diagonal count")
+        dev = H.vals.device
+        stride = round_stride(self.n)
+        self._vals = [torch.zeros((self.cap, stride), dtype=torch.float32, device=dev)
+                      for _ in range(2)]
+        self._off = [torch.zeros(self.cap, dtype=torch.int32, device=dev) for _ in range(2)]
+        self._cnt = [torch.zeros(1, dtype=torch.int32, device=dev) for _ in range(2)]
+        self.reset()
+        self._ws = lib().dia_spmspm_device_workspace(self.n, self.cap, H.K, self.cap)
+        self._work = torch.empty(max(self._ws, 1), dtype=torch.uint8, device=dev)
+
+    def reset(self):
+        """Back to P_1 = H (device copies only)."""
+        H = self.H
+        w = min(self._vals[0].shape[1], H.stride)
+        self._vals[0][:H.K, :w] = H.vals[:, :w]
+        self._off[0][:H.K] = H.d_offsets
+        self._cnt[0].fill_(H.K)
+        self.k, self._cur = 1, 0
+
+    def step(self, stream=None):
+        a, b = self._cur, 1 - self._cur
+        H = self.H
+        with torch.cuda.device(H.vals.device):
+            check(lib().dia_spmspm_rows_device(
+                self.n, _dptr(self._off[a]), _dptr(self._cnt[a]), self.cap, _dptr(self._vals[a]),
+                self._vals[a].shape[1], _dptr(H.d_offsets), H.K, _dptr(H.vals), H.stride,
+                _dptr(self._off[b]), _dptr(self._cnt[b]), self.cap, _dptr(self._vals[b]),
+                self._vals[b].shape[1], _dptr(self._work), self._ws, _stream(stream)))
+        self._cur, self.k = b, self.k + 1
+
+    def count(self):
+        """Device tensor [1] holding the current power's diagonal count."""
+        return self._cnt[self._cur]
+
+    def power(self) -> DiaRows:
+        nc = int(self._cnt[self._cur].item())
+        if nc > self.cap:
+            raise DiaError(DIA_ERR_CAPACITY, f"PowerChain: P_{self.k} has {nc} diagonals, "
+                                             f"max_diags is {self.cap}")
+        d_off = self._off[self._cur][:nc]
+        return DiaRows(self.n, self.n, d_off.cpu().numpy().astype(np.int32), d_off,
+                       self._vals[self._cur][:nc], 0, self.n)
 
 
 class SpmspmPlan:

@@ -133,6 +133,26 @@ int cuda_fail(cudaError_t e, const char* what);
 int num_sms();
 int persistent_blocks(const void* kernel, int smem_bytes);
 
+/* Persistent pair-sum kernel over nOut output diagonals and rows
+ * [row_lo, row_hi) (spmspm.cu).  With nOut_dev the count is read on the
+ * device and nOut is a capacity. */
+int launch_pair_sum(const float* U, const float* V, float* O, const OutDesc* outs,
+                    const Term* terms, int nOut, int row_lo, int row_hi, bool accumulate,
+                    cudaStream_t stream, float avg_terms = -1.0f,
+                    const int* nOut_dev = nullptr);
+
+/* Term lists of a rows-layout product written into caller buffers (terms:
+ * nC * nA slots, outs: nC), built on the device in A storage order
+ * (spmspm.cu).  With nA_dev / nC_dev the counts are read on the device and
+ * nA / nC are capacities. */
+int build_generic_terms_rows(long long n, const int* d_A_off, int nA, const int* d_B_off, int nB,
+                             const int* d_C_off, int nC, long long A_stride,
+                             long long B_stride, long long b_vrow0, long long b_lo,
+                             long long b_hi, long long C_stride, long long vrow0,
+                             long long row_lo, long long row_hi, Term* terms, OutDesc* outs,
+                             cudaStream_t stream, const int* nA_dev = nullptr,
+                             const int* nC_dev = nullptr);
+
 }  // namespace dia
 
 #define DIA_TRY_CUDA(expr)                                   \

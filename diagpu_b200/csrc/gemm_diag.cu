@@ -25,9 +25,6 @@
 
 namespace dia {
 
-int launch_pair_sum(const float* U, const float* V, float* O, const OutDesc* outs,
-                    const Term* terms, int nOut, int row_lo, int row_hi, bool accumulate,
-                    cudaStream_t stream, float avg_terms = -1.0f);
 int gemm_diag_tc_supported(const int* h_off_A, int P, const int* h_off_B, int Q, int n);
 int gemm_diag_tc_launch(const float* d_DA, const float* d_DB, const int* h_off_A, int P,
                         const int* h_off_B, int Q, int n, float* d_C_data,

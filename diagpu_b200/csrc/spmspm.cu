@@ -27,9 +27,6 @@
 
 namespace dia {
 
-int launch_pair_sum(const float* U, const float* V, float* O, const OutDesc* outs,
-                    const Term* terms, int nOut, int row_lo, int row_hi, bool accumulate,
-                    cudaStream_t stream, float avg_terms = -1.0f);
 
 /* A diagonal storage scheme reduced to "element offset of row 0" plus the
  * rows where the diagonal holds a stored value. */
@@ -70,6 +67,11 @@ struct PlanArgs {
     int stride_terms;     /* term slots per output diagonal (>= pairs) */
     Term* terms;
     OutDesc* outs;
+    /* optional device-resident counts (a device-side chain step): nA and nC
+     * above are then capacities; output diagonals past the device count
+     * get an empty descriptor */
+    const int* nA_dev;
+    const int* nC_dev;
 };
 
 constexpr int kBoffSmem = 2048;
@@ -84,8 +86,14 @@ __global__ void __launch_bounds__(kBlock) pair_plan_kernel(PlanArgs p)
         for (int b = tid; b < p.nB; b += kBlock) s_boff[b] = p.B_off[b];
     __syncthreads();
     const int n = p.A.n;
+    const int nA = p.nA_dev ? min(*p.nA_dev, p.nA) : p.nA;
+    const int nC = p.nC_dev ? min(*p.nC_dev, p.nC) : p.nC;
 
     for (int c = blockIdx.x; c < p.nC; c += gridDim.x) {
+        if (c >= nC) {
+            if (tid == 0) p.outs[c] = OutDesc{0, 0, 0, 0, 0, c * p.stride_terms, c * p.stride_terms};
+            continue;
+        }
         const int dc = p.C.off[c];
         OutDesc od;
         int olo, ohi;
@@ -104,11 +112,11 @@ __global__ void __launch_bounds__(kBlock) pair_plan_kernel(PlanArgs p)
         od.ohi = ohi;
         od.t0 = c * p.stride_terms;
         int count = 0;
-        for (int a0 = 0; a0 < p.nA; a0 += kBlock) {
+        for (int a0 = 0; a0 < nA; a0 += kBlock) {
             const int a = a0 + tid;
             bool valid = false;
             Term t;
-            if (a < p.nA && olo < ohi) {
+            if (a < nA && olo < ohi) {
                 const int da = p.A.off[a];
                 const long long db = (long long)dc - da;
                 int b = -1;
@@ -163,6 +171,7 @@ struct SumArgs {
     int row_hi;
     int ntiles;
     int tiles_per_item;  /* consecutive row tiles one work item covers */
+    const int* nOut_dev; /* optional device-resident count; nOut is then a capacity */
 };
 
 /* Persistent CTAs walk work items (output diagonal c, run of tiles), c
@@ -174,11 +183,12 @@ __global__ void __launch_bounds__(kBlock) pair_sum_kernel(SumArgs s)
 {
     constexpr int kTile = kBlock * ILP;
     __shared__ Term s_t[kMaxTerms];
+    const int nOut = s.nOut_dev ? min(*s.nOut_dev, s.nOut) : s.nOut;
     const int nchunks = (s.ntiles + s.tiles_per_item - 1) / s.tiles_per_item;
-    const long long items = (long long)s.nOut * nchunks;
+    const long long items = (long long)nOut * nchunks;
     for (long long it = blockIdx.x; it < items; it += gridDim.x) {
-        const int c = (int)(it % s.nOut);
-        const int tfirst = (int)(it / s.nOut) * s.tiles_per_item;
+        const int c = (int)(it % nOut);
+        const int tfirst = (int)(it / nOut) * s.tiles_per_item;
         const int tlast = min(s.ntiles, tfirst + s.tiles_per_item);
         const OutDesc od = s.outs[c];
         const int span_lo = s.row_lo + tfirst * kTile, span_hi = s.row_lo + tlast * kTile;
@@ -231,10 +241,12 @@ __global__ void __launch_bounds__(kBlock) pair_sum_kernel(SumArgs s)
 template <int ILP, int BATCH>
 static int launch_pair_sum_t(const float* U, const float* V, float* O, const OutDesc* outs,
                              const Term* terms, int nOut, int row_lo, int row_hi,
-                             bool accumulate, float avg_terms, cudaStream_t stream)
+                             bool accumulate, float avg_terms, cudaStream_t stream,
+                             const int* nOut_dev)
 {
     constexpr int kTile = kBlock * ILP;
-    SumArgs s{U, V, O, outs, terms, nOut, row_lo, row_hi, (row_hi - row_lo + kTile - 1) / kTile, 1};
+    SumArgs s{U, V, O, outs, terms, nOut, row_lo, row_hi, (row_hi - row_lo + kTile - 1) / kTile, 1,
+              nOut_dev};
     const void* k = accumulate ? (const void*)pair_sum_kernel<true, ILP, BATCH>
                                : (const void*)pair_sum_kernel<false, ILP, BATCH>;
     const long long slots = persistent_blocks(k, 0);
@@ -261,11 +273,11 @@ static int launch_pair_sum_t(const float* U, const float* V, float* O, const Out
  * rows [row_lo, row_hi). */
 int launch_pair_sum(const float* U, const float* V, float* O, const OutDesc* outs,
                     const Term* terms, int nOut, int row_lo, int row_hi, bool accumulate,
-                    cudaStream_t stream, float avg_terms)
+                    cudaStream_t stream, float avg_terms, const int* nOut_dev)
 {
     if (nOut <= 0 || row_hi <= row_lo) return DIA_OK;
     return launch_pair_sum_t<4, 4>(U, V, O, outs, terms, nOut, row_lo, row_hi, accumulate,
-                                   avg_terms, stream);
+                                   avg_terms, stream, nOut_dev);
 }
 
 static int run_planned(PlanArgs p, const float* U, const float* V, float* O,
@@ -297,10 +309,12 @@ int build_generic_terms_rows(long long n, const int* d_A_off, int nA, const int*
                              long long B_stride, long long b_vrow0, long long b_lo,
                              long long b_hi, long long C_stride, long long vrow0,
                              long long row_lo, long long row_hi, Term* terms, OutDesc* outs,
-                             cudaStream_t stream)
+                             cudaStream_t stream, const int* nA_dev, const int* nC_dev)
 {
     const int in = (int)n;
     PlanArgs p{};
+    p.nA_dev = nA_dev;
+    p.nC_dev = nC_dev;
     p.A = LayoutDesc{0, d_A_off, nullptr, nullptr, nullptr, A_stride, vrow0, (int)vrow0,
                      (int)std::min<long long>(vrow0 + A_stride, n), in};
     p.B = LayoutDesc{0, d_B_off, nullptr, nullptr, nullptr, B_stride, b_vrow0,

@@ -48,9 +48,6 @@ int runpair_launch(const RunPairPlan* rp, const float* A, const float* B, float*
                    long long thi, cudaStream_t stream);
 int runpair_tile_rows();
 
-int launch_pair_sum(const float* U, const float* V, float* O, const OutDesc* outs,
-                    const Term* terms, int nOut, int row_lo, int row_hi, bool accumulate,
-                    cudaStream_t stream, float avg_terms = -1.0f);
 
 constexpr int kClusterSpan = 64;       /* max span of one A-offset cluster */
 constexpr int kTileSmemCap = 100 * 1024;
@@ -183,16 +180,6 @@ long long mod4(long long x) { return ((x % 4) + 4) % 4; }
 
 }  // namespace
 
-namespace dia {
-/* device term lists of the generic path for a rows-layout product (the
- * same construction as dia_spmspm_rows; kept in the plan). */
-int build_generic_terms_rows(long long n, const int* d_A_off, int nA, const int* d_B_off, int nB,
-                             const int* d_C_off, int nC, long long A_stride,
-                             long long B_stride, long long b_vrow0, long long b_lo,
-                             long long b_hi, long long C_stride, long long vrow0,
-                             long long row_lo, long long row_hi, Term* terms, OutDesc* outs,
-                             cudaStream_t stream);
-}
 
 extern "C" int dia_spmspm_plan_create(int64_t n, const int* h_A_off, int nA, const int* h_B_off,
                                       int nB, int64_t A_stride, int64_t B_stride,

@@ -165,6 +165,35 @@ int dia_spmspm_plan_execute(const DiaSpmspmPlan* plan, const float* d_A_vals,
                             int64_t row_hi, int use_tiles, cudaStream_t stream);
 int dia_spmspm_plan_destroy(DiaSpmspmPlan* plan);
 
+/* Device-side steps for matrix-power chains (P_{k+1} = P_k * H with H
+ * narrow).  The reference resolves a chain step's pairs on the device but
+ * takes its output offsets from a host symbolic phase
+ * (spmspm/gather_flat.cuh:110-117); these calls keep the whole step on the
+ * device, so a chain runs without any host synchronisation:
+ *   - A's offsets and count live in device memory (d_A_off, d_nA; nA_cap is
+ *     their capacity), as the previous step left them; B's count nB is a
+ *     host value (H does not change);
+ *   - the output offsets are written ascending to d_C_off and their number
+ *     to d_nC -- the sumset of A's and B's offsets inside (-n, n), equal to
+ *     dia_spmspm_symbolic's C_off bit for bit.  If the number exceeds nC_cap
+ *     only the first nC_cap offsets are written and *d_nC still holds the
+ *     full number: the caller checks *d_nC <= nC_cap before using C;
+ *   - d_work is caller device memory of dia_spmspm_device_workspace() bytes
+ *     (a bitmap of the 2n-1 offsets, scan scratch and the term lists).
+ * dia_spmspm_rows_device also computes C = A*B on the rows layout with all
+ * n rows present (vrow0 = 0, strides >= n); values equal dia_spmspm_rows'
+ * bit for bit (same pair order: A storage order). */
+int64_t dia_spmspm_device_workspace(int64_t n, int nA_cap, int nB, int nC_cap);
+int dia_spmspm_symbolic_device(int64_t n, const int* d_A_off, const int* d_nA, int nA_cap,
+                               const int* d_B_off, int nB, int* d_C_off, int* d_nC,
+                               int nC_cap, void* d_work, int64_t work_bytes,
+                               cudaStream_t stream);
+int dia_spmspm_rows_device(int64_t n, const int* d_A_off, const int* d_nA, int nA_cap,
+                           const float* d_A_vals, int64_t A_stride, const int* d_B_off,
+                           int nB, const float* d_B_vals, int64_t B_stride, int* d_C_off,
+                           int* d_nC, int nC_cap, float* d_C_vals, int64_t C_stride,
+                           void* d_work, int64_t work_bytes, cudaStream_t stream);
+
 /* ----------------------------------------------------------- gemm_diag */
 
 /* C += A*B with gemm_diag_kernel's argument set (gemm_diag/gemm_diag.cu:
