@@ -281,6 +281,15 @@ def single_gpu_extras(dg, steps, warmup, hbm, src):
                 "ms": round(ms, 4), "bytes": byts,
                 "roofline": roofline(byts / ms / 1e6, hbm, src),
                 "host_planned_ms": round(ms_host, 4)})
+    # truncated-Taylor exp(tA) x of the config-1 operator: 16 chained SpMV terms
+    fn, byts = _only_taylor(dg)
+    ms = timed(fn, max(3, steps // 5), min(warmup, 3), flush=flush, per_launch=True)
+    out.append({"workload": f"config1 operator exp(tA)x, truncated Taylor, {TAYLOR_M} fused "
+                            "SpMV+scale+sum terms (L2 flushed per call)",
+                "metric": "taylor_GBps", "value": round(byts / ms / 1e6, 1), "unit": "GB/s",
+                "ms": round(ms, 4), "bytes": byts,
+                "roofline": roofline(byts / ms / 1e6, hbm, src),
+                "gpu_launches_per_step": TAYLOR_M})
     return out
 
 
@@ -549,6 +558,19 @@ CHAIN_K = 8
 CHAIN_OFF = np.array([-1024, -1, 0, 1, 1024], np.int32)
 
 
+TAYLOR_M = 16
+
+
+def _only_taylor(dg, n=1 << 20, m=TAYLOR_M):
+    """exp(tA) x of the config-1 operator by m chained SpMV terms."""
+    A = dg.DiaRows.synth(n, n, CHAIN_OFF, seed=101, base=[-1, -1, 4, -1, -1], lo=-0.01, hi=0.01)
+    x = dg.synth_vector(n, seed=102)
+    y = torch.empty(n, device="cuda")
+    work = torch.empty(2 * n, device="cuda")
+    byts = m * 4 * (nnz_rows(n, CHAIN_OFF, 0, n) + 4 * n) + 8 * n
+    return (lambda: dg.expm_taylor(A, 0.01, m, x, y, work=work)), byts
+
+
 def _only_chain(dg, host=False, n=1 << 20, k=CHAIN_K):
     """H^k of the config-1 operator: k-1 products P_{j+1} = P_j * H."""
     H = dg.DiaRows.synth(n, n, CHAIN_OFF, SEED_A)
@@ -581,6 +603,7 @@ ONLY = {
     "spmspm3": lambda dg: _only_spmspm(dg, 1_000_000, _scat(301), _scat(302), kind=1),
     "gemm4": lambda dg: _only_gemm4(dg),
     "chain1": lambda dg: _only_chain(dg),
+    "taylor1": lambda dg: _only_taylor(dg),
     "chain1_host": lambda dg: _only_chain(dg, host=True),
     "gemm4_simt": lambda dg: _only_gemm4(dg, mode=1),
 }

@@ -84,6 +84,8 @@ def lib():
         L.dia_device_status.restype = i
         L.dia_synth_rows.argtypes = [u64, i64, i64, i, p, p, i, f, f, i64, i64, i64, p, p]
         L.dia_synth_vector.argtypes = [u64, i64, i64, f, f, p, p]
+        L.dia_expm_taylor.argtypes = [i64, i, p, p, i64, f, i, p, p, p, p]
+        L.dia_expm_taylor.restype = i
         L.dia_spmspm_device_workspace.argtypes = [i64, i, i, i]
         L.dia_spmspm_device_workspace.restype = i64
         L.dia_spmspm_symbolic_device.argtypes = [i64, p, p, i, p, i, p, p, i, p, i64, p]
@@ -278,6 +280,24 @@ def spmspm_hm(A_values, A_starts, A_off, A_len, B_values, B_starts, B_len, B_loo
                               _dptr(C_starts, torch.int64), _dptr(C_off, torch.int32),
                               _dptr(C_len, torch.int32), C_off.numel(), n, _stream(stream)))
     return C_values
+
+
+def expm_taylor(A: DiaRows, t, m, x, y=None, *, work=None, stream=None):
+    """y = sum_{j=0}^{m} (tA)^j x / j!  (truncated Taylor series of exp(tA) x),
+    one fused SpMV + scale + running-sum launch per term (dia_expm_taylor).
+    A is a whole square matrix (vrow0 = 0); work (2n floats) may be passed
+    to reuse scratch across calls, e.g. under CUDA graph capture."""
+    if A.vrow0 != 0 or A.nrows != A.n_rows or A.n_rows != A.n_cols:
+        raise DiaError(DIA_ERR_INVALID, "expm_taylor: A must be a whole square matrix")
+    n = A.n_rows
+    y = torch.empty(n, dtype=torch.float32, device=x.device) if y is None else y
+    work = torch.empty(2 * n, dtype=torch.float32, device=x.device) if work is None else work
+    with torch.cuda.device(x.device):
+        check(lib().dia_expm_taylor(n, A.K, _dptr(A.d_offsets), _dptr(A.vals), A.stride,
+                                    float(t), int(m), _dptr(x, torch.float32),
+                                    _dptr(y, torch.float32), _dptr(work, torch.float32),
+                                    _stream(stream)))
+    return y
 
 
 def spmspm_symbolic_device(n, d_A_off, d_nA, nA_cap, d_B_off, nC_cap, *, stream=None):

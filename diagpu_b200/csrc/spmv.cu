@@ -35,9 +35,11 @@ struct SpmvArgs {
     int u_shift_by_d;     /* 1: value of row i at vals[.. + i + d] (Recon) */
     long long x_base;     /* x element of column c is x[c - x_base] */
     long long y_base;     /* y element of row i is y[i - y_base] */
+    float scale;          /* EPI: y = scale * (A x) and sum += y */
+    float* sum;
 };
 
-template <bool STREAM>
+template <bool STREAM, bool EPI = false>
 __global__ void __launch_bounds__(kBlock) spmv_kernel(SpmvArgs a)
 {
     __shared__ Term s_t[kMaxTerms];
@@ -72,7 +74,15 @@ __global__ void __launch_bounds__(kBlock) spmv_kernel(SpmvArgs a)
 #pragma unroll
     for (int j = 0; j < kILP; ++j) {
         const int i = r0 + j * kBlock;
-        if (i < a.row_hi) a.y[i - a.y_base] = acc[j];
+        if (i < a.row_hi) {
+            if (EPI) {
+                const float v = __fmul_rn(a.scale, acc[j]);
+                a.y[i - a.y_base] = v;
+                a.sum[i - a.y_base] = __fadd_rn(a.sum[i - a.y_base], v);
+            } else {
+                a.y[i - a.y_base] = acc[j];
+            }
+        }
     }
 }
 
@@ -81,7 +91,10 @@ static int launch_spmv(const SpmvArgs& a, cudaStream_t stream)
     const long long rows = (long long)a.row_hi - a.row_lo;
     if (rows <= 0) return DIA_OK;
     const long long grid = (rows + kTile - 1) / kTile;
-    spmv_kernel<true><<<(unsigned)grid, kBlock, 0, stream>>>(a);
+    if (a.sum)
+        spmv_kernel<true, true><<<(unsigned)grid, kBlock, 0, stream>>>(a);
+    else
+        spmv_kernel<true><<<(unsigned)grid, kBlock, 0, stream>>>(a);
     DIA_TRY_CUDA(cudaGetLastError());
     return DIA_OK;
 }
@@ -161,4 +174,49 @@ void launch_tc_spmv_regdirect(ReconView R, const float* d_x, int x_size, float* 
 {
     dia_spmv_recon(R.rows, R.cols, R.num_diags, R.diag_offsets, R.values, d_x, x_size, d_y,
                    stream);
+}
+
+/* Truncated Taylor series of exp(tA) x on the rows layout (whole matrix):
+ *     v_0 = x,  v_j = (t / j) * (A v_{j-1}),  y = v_0 + v_1 + ... + v_m,
+ * one fused launch per term (SpMV, scale, running sum), so y stays in HBM
+ * and each term costs 4*(nnz + 4n) bytes.  Rounding per element: the SpMV
+ * sum in offset storage order, then fl(c_j * s) with c_j = fl(t / j), then
+ * fl(y + v_j) -- the order of the CPU restatement in the oracle. */
+extern "C" int dia_expm_taylor(int64_t n, int num_diags, const int* d_offsets, const float* d_vals,
+                               int64_t stride, float t, int m, const float* d_x, float* d_y,
+                               float* d_work, cudaStream_t stream)
+{
+    if (n < 0 || num_diags < 0 || m < 0 || stride < n)
+        return fail(DIA_ERR_INVALID, "dia_expm_taylor: bad sizes (stride must be >= n)");
+    if (n == 0) return DIA_OK;
+    if (!d_x || !d_y || (m > 0 && (!d_work || (num_diags > 0 && (!d_offsets || !d_vals)))))
+        return fail(DIA_ERR_INVALID, "dia_expm_taylor: null pointer");
+    if (n + kTile >= (1LL << 31))
+        return fail(DIA_ERR_UNSUPPORTED, "dia_expm_taylor: n beyond int32 range");
+    DIA_TRY_CUDA(cudaMemcpyAsync(d_y, d_x, (size_t)n * 4, cudaMemcpyDeviceToDevice, stream));
+    const float* v = d_x;
+    for (int j = 1; j <= m; ++j) {
+        float* vn = d_work + (size_t)(j & 1) * (size_t)n;
+        SpmvArgs a{};
+        a.vals = d_vals;
+        a.x = v;
+        a.y = vn;
+        a.off = d_offsets;
+        a.K = num_diags;
+        a.row_lo = 0;
+        a.row_hi = (int)n;
+        a.clo = 0;
+        a.chi = (int)n;
+        a.u_row0 = 0;
+        a.u_kstride = stride;
+        a.u_shift_by_d = 0;
+        a.x_base = 0;
+        a.y_base = 0;
+        a.scale = t / (float)j;
+        a.sum = d_y;
+        const int rc = launch_spmv(a, stream);
+        if (rc) return rc;
+        v = vn;
+    }
+    return DIA_OK;
 }

@@ -165,6 +165,17 @@ int dia_spmspm_plan_execute(const DiaSpmspmPlan* plan, const float* d_A_vals,
                             int64_t row_hi, int use_tiles, cudaStream_t stream);
 int dia_spmspm_plan_destroy(DiaSpmspmPlan* plan);
 
+/* Truncated Taylor series of exp(tA) x for a whole square matrix A on the
+ * rows layout (stride >= n): v_0 = x, v_j = (t/j) * A v_{j-1}, y = sum of
+ * v_0 .. v_m.  One fused kernel per term (SpMV, scale, running sum); d_work
+ * holds 2n floats.  Per element: the SpMV sum in offset storage order, then
+ * fl(fl(t/j) * s), then fl(y + v_j), the order of the CPU oracle.  The
+ * reference has no such driver (its SpMV is a single product); this chains
+ * its SpMV into the time evolution its Hamiltonians are built for. */
+int dia_expm_taylor(int64_t n, int num_diags, const int* d_offsets, const float* d_vals,
+                    int64_t stride, float t, int m, const float* d_x, float* d_y,
+                    float* d_work, cudaStream_t stream);
+
 /* Device-side steps for matrix-power chains (P_{k+1} = P_k * H with H
  * narrow).  The reference resolves a chain step's pairs on the device but
  * takes its output offsets from a host symbolic phase

@@ -41,6 +41,7 @@ def lib():
         L.orc_spmv_recon.argtypes = [i, i, i, _i32p, _f32p, _f32p, i, _f32p]
         L.orc_spmv_csr.argtypes = [i, _i32p, _i32p, _f32p, _f32p, _f32p]
         L.orc_spmv_rowidx.argtypes = [i64, i64, i64, i, _i32p, _f32p, i64, _f32p, i64, i64, _f32p, i]
+        L.orc_expm_taylor.argtypes = [i64, i, _i32p, _f32p, i64, f, i, _f32p, _f32p, i]
         L.orc_c_structure.argtypes = [i, _i32p, i, _i32p, i, p, p, p]
         L.orc_c_structure.restype = i
         L.orc_pair_lists.argtypes = [i, _i32p, i, _i32p, i, _i32p, i, p, p, p]
@@ -109,6 +110,16 @@ def spmv_rowidx(offsets, vals, stride, x, *, ncols, row0=0, nrows=None, x_lo=0, 
     x = _a(x, np.float32)
     lib().orc_spmv_rowidx(row0, nrows, ncols, K, _a(offsets, np.int32), vals, stride, x,
                           x_lo, x.size, y, nthreads or threads())
+    return y
+
+
+def expm_taylor(offsets, vals, stride, t, m, x, *, nthreads=None):
+    """y = sum_{j<=m} (tA)^j x / j! by the recurrence of orc_expm_taylor."""
+    x = _a(x, np.float32)
+    y = np.empty(x.size, np.float32)
+    lib().orc_expm_taylor(x.size, len(offsets), _a(offsets, np.int32),
+                          _a(vals, np.float32).reshape(-1), stride, float(t), int(m), x, y,
+                          nthreads or threads())
     return y
 
 

@@ -129,6 +129,36 @@ ORC_API void orc_spmv_rowidx(int64_t row0, int64_t nrows, int64_t ncols,
     }
 }
 
+/* Truncated Taylor series of exp(tA) x (the library's dia_expm_taylor): the
+ * reference has no such driver, so this is the definition the library
+ * follows, built from the SpMV loop above: v_0 = x, v_j = fl(t/j) * (A
+ * v_{j-1}) rounded per element, y = ((v_0 + v_1) + v_2) + ... element by
+ * element.  A is a whole square matrix on the row-indexed layout. */
+ORC_API void orc_expm_taylor(int64_t n, int K, const int* offsets, const float* vals,
+                             int64_t stride, float t, int m, const float* x, float* y,
+                             int threads)
+{
+    float* v = (float*)malloc((size_t)n * sizeof(float));
+    float* w = (float*)malloc((size_t)n * sizeof(float));
+    memcpy(v, x, (size_t)n * sizeof(float));
+    memcpy(y, x, (size_t)n * sizeof(float));
+    for (int j = 1; j <= m; ++j) {
+        const float c = t / (float)j;
+        orc_spmv_rowidx(0, n, n, K, offsets, vals, stride, v, 0, n, w, threads);
+#pragma omp parallel for schedule(static) num_threads(threads > 0 ? threads : 1)
+        for (int64_t i = 0; i < n; ++i) {
+            const float q = c * w[i];
+            w[i] = q;
+            y[i] = y[i] + q;
+        }
+        float* tmp = v;
+        v = w;
+        w = tmp;
+    }
+    free(v);
+    free(w);
+}
+
 /* ------------------------------------------------------------------------
  * SpMSpM symbolic phase
  * ------------------------------------------------------------------------ */

@@ -92,3 +92,25 @@ def test_synth_deterministic_and_partition_free():
     assert np.abs(full).max() <= 1.0
     nrm = oracle.synth_rowidx(9, 20000, 20000, [0], kind=1, lo=0.0, hi=1.0)[0, :20000]
     assert abs(nrm.mean()) < 0.05 and abs(nrm.std() - 1.0) < 0.05
+
+
+def test_expm_taylor_oracle_matches_matrix_exponential():
+    """The Taylor recurrence the library follows converges to exp(tA) x
+    (scipy's expm on the dense matrix), so the definition is pinned."""
+    import scipy.linalg as sl
+    rng = np.random.default_rng(0)
+    n, stride = 96, 96
+    offs = np.array([-8, -1, 0, 1, 8], np.int32)
+    vals = np.zeros((len(offs), stride), np.float32)
+    A = np.zeros((n, n))
+    for k, d in enumerate(offs):
+        lo, hi = max(0, -d), min(n, n - d)
+        vals[k, lo:hi] = rng.uniform(-1, 1, hi - lo)
+        A[np.arange(lo, hi), np.arange(lo, hi) + d] = vals[k, lo:hi]
+    x = rng.uniform(-1, 1, n).astype(np.float32)
+    for t, m in ((0.1, 12), (0.5, 20)):
+        y = oracle.expm_taylor(offs, vals, stride, t, m, x)
+        ref = sl.expm(t * A) @ x
+        assert np.linalg.norm(y - ref) / np.linalg.norm(ref) < 1e-6
+    # m = 0 is the identity
+    assert np.array_equal(oracle.expm_taylor(offs, vals, stride, 0.3, 0, x), x)
