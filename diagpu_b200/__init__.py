@@ -84,6 +84,8 @@ def lib():
         L.dia_device_status.restype = i
         L.dia_synth_rows.argtypes = [u64, i64, i64, i, p, p, i, f, f, i64, i64, i64, p, p]
         L.dia_synth_vector.argtypes = [u64, i64, i64, f, f, p, p]
+        L.dia_mtx_read.argtypes = [C.c_char_p, p, p, p, p, p, i64]
+        L.dia_mtx_read.restype = i
         L.dia_expm_taylor.argtypes = [i64, i, p, p, i64, f, i, p, p, p, p]
         L.dia_expm_taylor.restype = i
         L.dia_spmspm_device_workspace.argtypes = [i64, i, i, i]
@@ -280,6 +282,32 @@ def spmspm_hm(A_values, A_starts, A_off, A_len, B_values, B_starts, B_len, B_loo
                               _dptr(C_starts, torch.int64), _dptr(C_off, torch.int32),
                               _dptr(C_len, torch.int32), C_off.numel(), n, _stream(stream)))
     return C_values
+
+
+def read_mtx_host(path):
+    """Parse a Matrix Market coordinate file into the rows layout on the host
+    (dia_mtx_read; no GPU needed).  Returns (n_rows, n_cols, offsets int32
+    [K], vals float32 [K, stride]) with stride = round_stride(n_rows)."""
+    L = lib()
+    bpath = os.fsencode(path)
+    nr, nc, K = C.c_int64(0), C.c_int64(0), C.c_int(0)
+    check(L.dia_mtx_read(bpath, C.byref(nr), C.byref(nc), C.byref(K), None, None, 0))
+    offs = np.empty(max(K.value, 1), np.int32)
+    stride = round_stride(nr.value)
+    vals = np.empty((max(K.value, 1), stride), np.float32)
+    check(L.dia_mtx_read(bpath, C.byref(nr), C.byref(nc), C.byref(K),
+                         offs.ctypes.data_as(C.c_void_p), vals.ctypes.data_as(C.c_void_p),
+                         stride))
+    return nr.value, nc.value, offs[:K.value], vals[:K.value]
+
+
+def read_mtx(path, *, device="cuda") -> DiaRows:
+    """A Matrix Market coordinate file as a whole-matrix DiaRows on the GPU."""
+    n_rows, n_cols, offs, vals = read_mtx_host(path)
+    A = DiaRows.empty(n_rows, n_cols, offs, device=device)
+    if len(offs):
+        A.vals.copy_(torch.from_numpy(vals))
+    return A
 
 
 def expm_taylor(A: DiaRows, t, m, x, y=None, *, work=None, stream=None):

@@ -165,6 +165,18 @@ int dia_spmspm_plan_execute(const DiaSpmspmPlan* plan, const float* d_A_vals,
                             int64_t row_hi, int use_tiles, cudaStream_t stream);
 int dia_spmspm_plan_destroy(DiaSpmspmPlan* plan);
 
+/* Matrix Market ingestion (host only, no GPU needed): a coordinate file
+ * (real / double / integer / pattern; general / symmetric / skew-symmetric)
+ * such as spmv/tools/gen_banded_mtx.cpp writes, laid out as the rows layout:
+ * offsets j - i ascending, h_vals[k*stride + i] = A[i, i + off[k]], zero
+ * elsewhere (duplicates summed in double in file order, one rounding to
+ * fp32).  Two calls: with h_offsets = h_vals = NULL it parses and returns
+ * the shape and *num_diags; then with buffers (*num_diags = their capacity,
+ * stride >= n_rows) it fills them.  DIA_ERR_UNSUPPORTED for array or
+ * complex files. */
+int dia_mtx_read(const char* path, int64_t* n_rows, int64_t* n_cols, int* num_diags,
+                 int* h_offsets, float* h_vals, int64_t stride);
+
 /* Truncated Taylor series of exp(tA) x for a whole square matrix A on the
  * rows layout (stride >= n): v_0 = x, v_j = (t/j) * A v_{j-1}, y = sum of
  * v_0 .. v_m.  One fused kernel per term (SpMV, scale, running sum); d_work

@@ -25,11 +25,16 @@ benchmark generators:
   gemm_diag.npz      pack_diag_matrix(n, -hb..hb, 42/137) of
                      gemm_diag/gemm_diag.cu:361-382,485-486; build_c_layout;
                      cpu_diag_multiply (dense, mapped to the HM layout).
+  banded_64.mtx      the Matrix Market file spmv/tools/gen_banded_mtx.cpp
+                     writes for n = 64 (its SpMV benchmark's banded matrix),
+                     from the generator compiled unmodified into
+                     oracle/_ref/gen_banded_mtx.
 """
 from __future__ import annotations
 
 import ctypes as C
 import os
+import subprocess
 import re
 import sys
 
@@ -256,6 +261,13 @@ def gemm_diag(lib):
     np.savez(os.path.join(OUT, "gemm_diag.npz"), names=np.array([c[0] for c in cases]), **out)
 
 
+def banded_mtx(n=64):
+    """The reference's gen_banded_mtx output (Matrix Market text) for n rows."""
+    exe = os.path.join(os.path.dirname(oracle.__file__), "_ref", "gen_banded_mtx")
+    path = os.path.join(OUT, f"banded_{n}.mtx")
+    subprocess.run([exe, str(n), path], check=True, capture_output=True)
+
+
 def main():
     s = oracle.ref("spmv")
     m = oracle.ref("spmspm")
@@ -268,8 +280,9 @@ def main():
     spmspm_banded(m)
     spmspm_scatter(m)
     gemm_diag(g)
+    banded_mtx()
     for f in sorted(os.listdir(OUT)):
-        if f.endswith(".npz"):
+        if f.endswith((".npz", ".mtx")):
             print(f, os.path.getsize(os.path.join(OUT, f)))
 
 

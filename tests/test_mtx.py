@@ -1,0 +1,117 @@
+"""Matrix Market ingestion (dia_mtx_read, host side: runs without a GPU).
+
+The golden file is the reference's own generator output
+(spmv/tools/gen_banded_mtx.cpp, compiled unmodified; see
+tests/golden/make_golden.py); scipy.io.mmread is the independent reader the
+results are compared with, entry for entry."""
+import ctypes as C
+import os
+import warnings
+
+import numpy as np
+import pytest
+import scipy.io as sio
+
+import diagpu_b200 as dg
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def _dense_from_rows(n_rows, n_cols, offs, vals):
+    A = np.zeros((n_rows, n_cols), np.float32)
+    for k, d in enumerate(offs):
+        for i in range(n_rows):
+            j = i + int(d)
+            if 0 <= j < n_cols:
+                A[i, j] = vals[k, i]
+            else:
+                assert vals[k, i] == 0.0          # out-of-matrix entries are zero
+        assert (vals[k, n_rows:] == 0.0).all()    # stride padding is zero
+    return A
+
+
+def _scipy_dense(path):
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore")
+        return np.asarray(sio.mmread(path).toarray(), np.float64).astype(np.float32)
+
+
+def test_golden_reference_generator_file():
+    path = os.path.join(GOLDEN, "banded_64.mtx")
+    n_rows, n_cols, offs, vals = dg.read_mtx_host(path)
+    assert (n_rows, n_cols) == (64, 64)
+    assert np.array_equal(offs, [-9, -5, -2, -1, 0, 1, 2, 5, 9])   # the generator's set
+    assert np.array_equal(_dense_from_rows(n_rows, n_cols, offs, vals), _scipy_dense(path))
+
+
+CASES = {
+    "symmetric": ("real symmetric", 5, 5,
+                  [(1, 1, 2.5), (3, 1, -1.25), (5, 2, 0.5), (4, 4, 7.0)]),
+    "skew": ("real skew-symmetric", 4, 4, [(2, 1, 3.0), (4, 3, -0.75)]),
+    "pattern": ("pattern general", 3, 6, [(1, 6), (2, 2), (3, 1)]),
+    "integer": ("integer general", 4, 4, [(1, 2, 7), (4, 1, -3), (2, 2, 11)]),
+    "duplicates": ("real general", 3, 3, [(1, 1, 0.1), (1, 1, 0.2), (2, 3, 1e-8), (2, 3, 1.0)]),
+    "rectangular": ("real general", 3, 7, [(1, 7, 1.5), (3, 1, -2.0), (2, 2, 0.125)]),
+}
+
+
+def _write(path, kind, m, n, entries, comments=True):
+    with open(path, "w") as f:
+        f.write(f"%%MatrixMarket matrix coordinate {kind}\n")
+        if comments:
+            f.write("% a comment\n%\n\n")
+        f.write(f"{m} {n} {len(entries)}\n")
+        for e in entries:
+            f.write(" ".join(str(x) for x in e) + "\n")
+
+
+@pytest.mark.parametrize("case", sorted(CASES))
+def test_formats_match_scipy(tmp_path, case):
+    kind, m, n, entries = CASES[case]
+    path = str(tmp_path / f"{case}.mtx")
+    _write(path, kind, m, n, entries)
+    n_rows, n_cols, offs, vals = dg.read_mtx_host(path)
+    assert (n_rows, n_cols) == (m, n)
+    assert np.all(np.diff(offs) > 0)               # ascending, distinct
+    assert np.array_equal(_dense_from_rows(n_rows, n_cols, offs, vals), _scipy_dense(path))
+
+
+@pytest.mark.parametrize("banner,code", [
+    ("%%MatrixMarket matrix array real general", dg.DIA_ERR_UNSUPPORTED),
+    ("%%MatrixMarket matrix coordinate complex general", dg.DIA_ERR_UNSUPPORTED),
+    ("%%MatrixMarket matrix coordinate real hermitian", dg.DIA_ERR_UNSUPPORTED),
+    ("%%NotMatrixMarket matrix coordinate real general", dg.DIA_ERR_INVALID),
+])
+def test_rejected_files(tmp_path, banner, code):
+    path = str(tmp_path / "bad.mtx")
+    with open(path, "w") as f:
+        f.write(banner + "\n2 2 1\n1 1 1.0\n")
+    with pytest.raises(dg.DiaError) as e:
+        dg.read_mtx_host(path)
+    assert e.value.code == code
+
+
+def test_malformed_entries(tmp_path):
+    for body, name in (("3 3 2\n1 1 1.0\n", "truncated"), ("3 3 1\n4 1 1.0\n", "outside"),
+                       ("3 3 1\n1 1\n", "no value"), ("x y z\n", "size line")):
+        path = str(tmp_path / "m.mtx")
+        with open(path, "w") as f:
+            f.write("%%MatrixMarket matrix coordinate real general\n" + body)
+        with pytest.raises(dg.DiaError) as e:
+            dg.read_mtx_host(path)
+        assert e.value.code == dg.DIA_ERR_INVALID, name
+    with pytest.raises(dg.DiaError):
+        dg.read_mtx_host(str(tmp_path / "missing.mtx"))
+
+
+def test_capacity_two_call_pattern():
+    L = dg.lib()
+    path = os.fsencode(os.path.join(GOLDEN, "banded_64.mtx"))
+    nr, nc, K = C.c_int64(0), C.c_int64(0), C.c_int(0)
+    assert L.dia_mtx_read(path, C.byref(nr), C.byref(nc), C.byref(K), None, None, 0) == 0
+    assert K.value == 9
+    small = C.c_int(4)
+    offs = np.empty(4, np.int32)
+    rc = L.dia_mtx_read(path, C.byref(nr), C.byref(nc), C.byref(small),
+                        offs.ctypes.data_as(C.c_void_p), None, 0)
+    assert rc == dg.DIA_ERR_CAPACITY and small.value == 9
