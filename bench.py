@@ -290,6 +290,13 @@ def single_gpu_extras(dg, steps, warmup, hbm, src):
                 "ms": round(ms, 4), "bytes": byts,
                 "roofline": roofline(byts / ms / 1e6, hbm, src),
                 "gpu_launches_per_step": TAYLOR_M})
+    # complex64 SpMV (Hamiltonian-type operators), 27-point stencil on 256^3
+    fn, byts = _only_spmv_c64(dg)
+    ms = timed(fn, max(3, steps // 5), min(warmup, 3))
+    out.append({"workload": "complex64 DIA SpMV, 27-pt stencil 256^3 (n=16.8M, inputs > L2)",
+                "metric": "spmv_c64_GBps", "value": round(byts / ms / 1e6, 1), "unit": "GB/s",
+                "ms": round(ms, 4), "bytes": byts,
+                "roofline": roofline(byts / ms / 1e6, hbm, src)})
     return out
 
 
@@ -571,6 +578,19 @@ def _only_taylor(dg, n=1 << 20, m=TAYLOR_M):
     return (lambda: dg.expm_taylor(A, 0.01, m, x, y, work=work)), byts
 
 
+def _only_spmv_c64(dg, n=256 * 256 * 256):
+    """complex64 SpMV, 27-point stencil offsets on a 256^3 grid (inputs > L2)."""
+    A = dg.DiaRows.empty(n, n, OFF5, dtype=torch.complex64, zero=False)
+    re = dg.DiaRows.synth(n, n, OFF5, SEED_A)
+    A.vals.real.copy_(re.vals)
+    A.vals.imag.copy_(dg.DiaRows.synth(n, n, OFF5, SEED_A + 1).vals)
+    del re
+    x = torch.complex(dg.synth_vector(n, SEED_X), dg.synth_vector(n, SEED_X + 1))
+    y = torch.empty(n, dtype=torch.complex64, device="cuda")
+    byts = 8 * (nnz_rows(n, OFF5, 0, n) + 2 * n)
+    return (lambda: dg.spmv_c64(A, x, y)), byts
+
+
 def _only_chain(dg, host=False, n=1 << 20, k=CHAIN_K):
     """H^k of the config-1 operator: k-1 products P_{j+1} = P_j * H."""
     H = dg.DiaRows.synth(n, n, CHAIN_OFF, SEED_A)
@@ -604,6 +624,7 @@ ONLY = {
     "gemm4": lambda dg: _only_gemm4(dg),
     "chain1": lambda dg: _only_chain(dg),
     "taylor1": lambda dg: _only_taylor(dg),
+    "spmvc": lambda dg: _only_spmv_c64(dg),
     "chain1_host": lambda dg: _only_chain(dg, host=True),
     "gemm4_simt": lambda dg: _only_gemm4(dg, mode=1),
 }

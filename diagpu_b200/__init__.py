@@ -84,6 +84,10 @@ def lib():
         L.dia_device_status.restype = i
         L.dia_synth_rows.argtypes = [u64, i64, i64, i, p, p, i, f, f, i64, i64, i64, p, p]
         L.dia_synth_vector.argtypes = [u64, i64, i64, f, f, p, p]
+        L.dia_spmv_rows_c64.argtypes = [i64, i64, i, p, p, i64, p, p, p]
+        L.dia_expm_taylor_c64.argtypes = [i64, i, p, p, i64, f, i, p, p, p, p]
+        for name in ("dia_spmv_rows_c64", "dia_expm_taylor_c64"):
+            getattr(L, name).restype = i
         L.dia_mtx_read.argtypes = [C.c_char_p, p, p, p, p, p, i64]
         L.dia_mtx_read.restype = i
         L.dia_expm_taylor.argtypes = [i64, i, p, p, i64, f, i, p, p, p, p]
@@ -178,11 +182,14 @@ class DiaRows:
         return int(np.abs(self.offsets).max()) if self.K else 0
 
     @staticmethod
-    def empty(n_rows, n_cols, offsets, *, vrow0=0, nrows=None, device="cuda", zero=True):
+    def empty(n_rows, n_cols, offsets, *, vrow0=0, nrows=None, device="cuda", zero=True,
+              dtype=torch.float32):
+        """dtype float32, or complex64 for the complex paths (spmv_c64,
+        expm_taylor_c64; stride then counts complex elements)."""
         offsets = np.ascontiguousarray(offsets, np.int32)
         nrows = n_rows - vrow0 if nrows is None else nrows
         alloc = torch.zeros if zero else torch.empty
-        vals = alloc((len(offsets), round_stride(nrows)), dtype=torch.float32, device=device)
+        vals = alloc((len(offsets), round_stride(nrows)), dtype=dtype, device=device)
         d_off = torch.from_numpy(offsets.copy()).to(device)
         return DiaRows(n_rows, n_cols, offsets, d_off, vals, vrow0, nrows)
 
@@ -204,10 +211,12 @@ class DiaRows:
 
     @staticmethod
     def from_host(n_rows, n_cols, offsets, vals_rows, *, vrow0=0, device="cuda"):
-        """From a host [K, nrows] array in rows layout (no padding needed)."""
-        vals_rows = np.asarray(vals_rows, np.float32)
+        """From a host [K, nrows] array in rows layout (no padding needed);
+        a complex array gives a complex64 matrix."""
+        cplx = np.iscomplexobj(vals_rows)
+        vals_rows = np.asarray(vals_rows, np.complex64 if cplx else np.float32)
         A = DiaRows.empty(n_rows, n_cols, offsets, vrow0=vrow0, nrows=vals_rows.shape[1],
-                          device=device)
+                          device=device, dtype=torch.complex64 if cplx else torch.float32)
         A.vals[:, :vals_rows.shape[1]] = torch.from_numpy(vals_rows).to(device)
         return A
 
@@ -282,6 +291,41 @@ def spmspm_hm(A_values, A_starts, A_off, A_len, B_values, B_starts, B_len, B_loo
                               _dptr(C_starts, torch.int64), _dptr(C_off, torch.int32),
                               _dptr(C_len, torch.int32), C_off.numel(), n, _stream(stream)))
     return C_values
+
+
+def _whole_c64(A, who):
+    if A.vals.dtype != torch.complex64:
+        raise DiaError(DIA_ERR_INVALID, f"{who}: A must hold complex64 values")
+    if A.vrow0 != 0 or A.nrows != A.n_rows:
+        raise DiaError(DIA_ERR_INVALID, f"{who}: A must be a whole matrix")
+
+
+def spmv_c64(A: DiaRows, x, y=None, *, stream=None):
+    """y = A x for a complex64 matrix and vector (dia_spmv_rows_c64)."""
+    _whole_c64(A, "spmv_c64")
+    y = torch.empty(A.n_rows, dtype=torch.complex64, device=x.device) if y is None else y
+    with torch.cuda.device(x.device):
+        check(lib().dia_spmv_rows_c64(A.n_rows, A.n_cols, A.K, _dptr(A.d_offsets), _dptr(A.vals),
+                                      A.stride, _dptr(x, torch.complex64),
+                                      _dptr(y, torch.complex64), _stream(stream)))
+    return y
+
+
+def expm_taylor_c64(A: DiaRows, t, m, x, y=None, *, work=None, stream=None):
+    """y = exp(-i t A) x by the truncated Taylor series of m terms
+    (dia_expm_taylor_c64), e.g. the time evolution of a Hamiltonian."""
+    _whole_c64(A, "expm_taylor_c64")
+    if A.n_rows != A.n_cols:
+        raise DiaError(DIA_ERR_INVALID, "expm_taylor_c64: A must be square")
+    n = A.n_rows
+    y = torch.empty(n, dtype=torch.complex64, device=x.device) if y is None else y
+    work = torch.empty(2 * n, dtype=torch.complex64, device=x.device) if work is None else work
+    with torch.cuda.device(x.device):
+        check(lib().dia_expm_taylor_c64(n, A.K, _dptr(A.d_offsets), _dptr(A.vals), A.stride,
+                                        float(t), int(m), _dptr(x, torch.complex64),
+                                        _dptr(y, torch.complex64),
+                                        _dptr(work, torch.complex64), _stream(stream)))
+    return y
 
 
 def read_mtx_host(path):

@@ -220,3 +220,158 @@ extern "C" int dia_expm_taylor(int64_t n, int num_diags, const int* d_offsets, c
     }
     return DIA_OK;
 }
+
+/* ------------------------------------------------------------ complex64 */
+
+namespace dia {
+
+/* complex fp32 multiply-add, rounding spelled out so the CPU oracle can
+ * follow it: re += fl(fl(ar*br) - fl(ai*bi)), im += fl(fl(ar*bi) + fl(ai*br)) */
+__device__ __forceinline__ void cmul_add(float2& acc, float2 a, float2 b)
+{
+    const float pr = __fsub_rn(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y));
+    const float pi = __fadd_rn(__fmul_rn(a.x, b.y), __fmul_rn(a.y, b.x));
+    acc.x = __fadd_rn(acc.x, pr);
+    acc.y = __fadd_rn(acc.y, pi);
+}
+
+struct SpmvC64Args {
+    const float2* vals;   /* [K][stride] */
+    const float2* x;
+    float2* y;
+    const int* off;
+    int K, n_rows, n_cols;
+    long long stride;
+    /* EPI: y = (-i c) * (A x) and sum += y  (a term of exp(-i t A) x) */
+    float c;
+    float2* sum;
+};
+
+constexpr int kC64Ilp = 2;
+constexpr int kC64Tile = kBlock * kC64Ilp;
+
+/* One CTA per tile of rows; terms (one per diagonal) staged in shared
+ * memory; lanes read consecutive rows of each diagonal (8-byte values,
+ * 256-byte coalesced runs) and the matching shifted x window. */
+template <bool EPI>
+__global__ void __launch_bounds__(kBlock) spmv_c64_kernel(SpmvC64Args a)
+{
+    __shared__ Term s_t[kMaxTerms];
+    const int tile_lo = (int)blockIdx.x * kC64Tile;
+    const int r0 = tile_lo + (int)threadIdx.x;
+    float2 acc[kC64Ilp];
+#pragma unroll
+    for (int j = 0; j < kC64Ilp; ++j) acc[j] = make_float2(0.0f, 0.0f);
+    for (int k0 = 0; k0 < a.K; k0 += kMaxTerms) {
+        const int nt = min(kMaxTerms, a.K - k0);
+        if (k0) __syncthreads();
+        for (int q = threadIdx.x; q < nt; q += kBlock) {
+            const int k = k0 + q;
+            const int d = a.off[k];
+            Term t;
+            t.u = (long long)k * a.stride;
+            t.v = d;
+            t.lo = max(0, -d);
+            t.hi = min(a.n_rows, a.n_cols - d);
+            if (t.hi < t.lo) t.hi = t.lo;
+            s_t[q] = t;
+        }
+        __syncthreads();
+        for (int q = 0; q < nt; ++q) {
+            const Term t = s_t[q];
+#pragma unroll
+            for (int j = 0; j < kC64Ilp; ++j) {
+                const int i = r0 + j * kBlock;
+                if (i >= t.lo && i < t.hi)
+                    cmul_add(acc[j], __ldcs(a.vals + t.u + i), __ldg(a.x + t.v + i));
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kC64Ilp; ++j) {
+        const int i = r0 + j * kBlock;
+        if (i >= a.n_rows) continue;
+        if (EPI) {
+            /* (-i c) * (s.x + i s.y) = c s.y - i c s.x */
+            const float2 v = make_float2(__fmul_rn(a.c, acc[j].y), -__fmul_rn(a.c, acc[j].x));
+            a.y[i] = v;
+            float2 s = a.sum[i];
+            s.x = __fadd_rn(s.x, v.x);
+            s.y = __fadd_rn(s.y, v.y);
+            a.sum[i] = s;
+        } else {
+            a.y[i] = acc[j];
+        }
+    }
+}
+
+static int launch_spmv_c64(const SpmvC64Args& a, cudaStream_t stream)
+{
+    if (a.n_rows <= 0) return DIA_OK;
+    const long long grid = ((long long)a.n_rows + kC64Tile - 1) / kC64Tile;
+    if (a.sum)
+        spmv_c64_kernel<true><<<(unsigned)grid, kBlock, 0, stream>>>(a);
+    else
+        spmv_c64_kernel<false><<<(unsigned)grid, kBlock, 0, stream>>>(a);
+    DIA_TRY_CUDA(cudaGetLastError());
+    return DIA_OK;
+}
+
+}  // namespace dia
+
+extern "C" int dia_spmv_rows_c64(int64_t n_rows, int64_t n_cols, int num_diags,
+                                 const int* d_offsets, const void* d_vals, int64_t stride,
+                                 const void* d_x, void* d_y, cudaStream_t stream)
+{
+    if (n_rows < 0 || n_cols < 0 || num_diags < 0 || stride < n_rows)
+        return fail(DIA_ERR_INVALID, "dia_spmv_rows_c64: bad sizes (stride must be >= n_rows)");
+    if (n_rows == 0) return DIA_OK;
+    if (!d_y || (num_diags > 0 && (!d_offsets || !d_vals || !d_x)))
+        return fail(DIA_ERR_INVALID, "dia_spmv_rows_c64: null pointer");
+    if (n_rows + kC64Tile >= (1LL << 31) || n_cols >= (1LL << 31))
+        return fail(DIA_ERR_UNSUPPORTED, "dia_spmv_rows_c64: dimensions beyond int32 range");
+    SpmvC64Args a{};
+    a.vals = (const float2*)d_vals;
+    a.x = (const float2*)d_x;
+    a.y = (float2*)d_y;
+    a.off = d_offsets;
+    a.K = num_diags;
+    a.n_rows = (int)n_rows;
+    a.n_cols = (int)n_cols;
+    a.stride = stride;
+    return launch_spmv_c64(a, stream);
+}
+
+extern "C" int dia_expm_taylor_c64(int64_t n, int num_diags, const int* d_offsets,
+                                   const void* d_vals, int64_t stride, float t, int m,
+                                   const void* d_x, void* d_y, void* d_work,
+                                   cudaStream_t stream)
+{
+    if (n < 0 || num_diags < 0 || m < 0 || stride < n)
+        return fail(DIA_ERR_INVALID, "dia_expm_taylor_c64: bad sizes (stride must be >= n)");
+    if (n == 0) return DIA_OK;
+    if (!d_x || !d_y || (m > 0 && (!d_work || (num_diags > 0 && (!d_offsets || !d_vals)))))
+        return fail(DIA_ERR_INVALID, "dia_expm_taylor_c64: null pointer");
+    if (n + kC64Tile >= (1LL << 31))
+        return fail(DIA_ERR_UNSUPPORTED, "dia_expm_taylor_c64: n beyond int32 range");
+    DIA_TRY_CUDA(cudaMemcpyAsync(d_y, d_x, (size_t)n * 8, cudaMemcpyDeviceToDevice, stream));
+    const float2* v = (const float2*)d_x;
+    for (int j = 1; j <= m; ++j) {
+        float2* vn = (float2*)d_work + (size_t)(j & 1) * (size_t)n;
+        SpmvC64Args a{};
+        a.vals = (const float2*)d_vals;
+        a.x = v;
+        a.y = vn;
+        a.off = d_offsets;
+        a.K = num_diags;
+        a.n_rows = (int)n;
+        a.n_cols = (int)n;
+        a.stride = stride;
+        a.c = t / (float)j;
+        a.sum = (float2*)d_y;
+        const int rc = launch_spmv_c64(a, stream);
+        if (rc) return rc;
+        v = vn;
+    }
+    return DIA_OK;
+}

@@ -165,6 +165,22 @@ int dia_spmspm_plan_execute(const DiaSpmspmPlan* plan, const float* d_A_vals,
                             int64_t row_hi, int use_tiles, cudaStream_t stream);
 int dia_spmspm_plan_destroy(DiaSpmspmPlan* plan);
 
+/* Complex64 (interleaved fp32 re, im) DIA on the rows layout, whole matrix
+ * (vrow0 = 0, stride in complex elements >= n_rows): y = A x with
+ * per-term rounding re += fl(fl(ar*xr) - fl(ai*xi)), im += fl(fl(ar*xi) +
+ * fl(ai*xr)) in offset storage order (with zero imaginary parts this is the
+ * real SpMV bit for bit).  dia_expm_taylor_c64 is the Schroedinger-type
+ * evolution y = exp(-i t A) x by the truncated Taylor series v_0 = x,
+ * v_j = (-i fl(t/j)) (A v_{j-1}), y = sum v_j, one fused launch per term;
+ * d_work holds 2n complex values.  The reference is real-only; these serve
+ * the complex Hamiltonians its DIA format targets. */
+int dia_spmv_rows_c64(int64_t n_rows, int64_t n_cols, int num_diags, const int* d_offsets,
+                      const void* d_vals, int64_t stride, const void* d_x, void* d_y,
+                      cudaStream_t stream);
+int dia_expm_taylor_c64(int64_t n, int num_diags, const int* d_offsets, const void* d_vals,
+                        int64_t stride, float t, int m, const void* d_x, void* d_y,
+                        void* d_work, cudaStream_t stream);
+
 /* Matrix Market ingestion (host only, no GPU needed): a coordinate file
  * (real / double / integer / pattern; general / symmetric / skew-symmetric)
  * such as spmv/tools/gen_banded_mtx.cpp writes, laid out as the rows layout:

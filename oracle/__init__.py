@@ -42,6 +42,8 @@ def lib():
         L.orc_spmv_csr.argtypes = [i, _i32p, _i32p, _f32p, _f32p, _f32p]
         L.orc_spmv_rowidx.argtypes = [i64, i64, i64, i, _i32p, _f32p, i64, _f32p, i64, i64, _f32p, i]
         L.orc_expm_taylor.argtypes = [i64, i, _i32p, _f32p, i64, f, i, _f32p, _f32p, i]
+        L.orc_spmv_rowidx_c64.argtypes = [i64, i64, i, _i32p, _f32p, i64, _f32p, _f32p, i]
+        L.orc_expm_taylor_c64.argtypes = [i64, i, _i32p, _f32p, i64, f, i, _f32p, _f32p, i]
         L.orc_c_structure.argtypes = [i, _i32p, i, _i32p, i, p, p, p]
         L.orc_c_structure.restype = i
         L.orc_pair_lists.argtypes = [i, _i32p, i, _i32p, i, _i32p, i, p, p, p]
@@ -121,6 +123,28 @@ def expm_taylor(offsets, vals, stride, t, m, x, *, nthreads=None):
                           _a(vals, np.float32).reshape(-1), stride, float(t), int(m), x, y,
                           nthreads or threads())
     return y
+
+
+def _c64_as_f32(a):
+    a = np.ascontiguousarray(a, np.complex64)
+    return a.view(np.float32).reshape(-1)
+
+
+def spmv_c64(offsets, vals, stride, x, *, n_rows, n_cols, nthreads=None):
+    """y = A x for complex64 A (rows layout [K, stride]) and x."""
+    y = np.empty(2 * n_rows, np.float32)
+    lib().orc_spmv_rowidx_c64(n_rows, n_cols, len(offsets), _a(offsets, np.int32),
+                              _c64_as_f32(vals), stride, _c64_as_f32(x), y, nthreads or threads())
+    return y.view(np.complex64)
+
+
+def expm_taylor_c64(offsets, vals, stride, t, m, x, *, nthreads=None):
+    """exp(-i t A) x by the truncated Taylor recurrence of orc_expm_taylor_c64."""
+    x = np.ascontiguousarray(x, np.complex64)
+    y = np.empty(2 * x.size, np.float32)
+    lib().orc_expm_taylor_c64(x.size, len(offsets), _a(offsets, np.int32), _c64_as_f32(vals),
+                              stride, float(t), int(m), _c64_as_f32(x), y, nthreads or threads())
+    return y.view(np.complex64)
 
 
 # ------------------------------------------------------------ SpMSpM symbolic

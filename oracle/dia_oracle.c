@@ -159,6 +159,66 @@ ORC_API void orc_expm_taylor(int64_t n, int K, const int* offsets, const float* 
     free(w);
 }
 
+/* Complex64 SpMV on the row-indexed layout (the library's
+ * dia_spmv_rows_c64; the reference is real-only): values and x interleaved
+ * (re, im); per term re += fl(fl(ar*xr) - fl(ai*xi)), im += fl(fl(ar*xi) +
+ * fl(ai*xr)), terms in offset storage order, whole square or rectangular
+ * matrix. */
+ORC_API void orc_spmv_rowidx_c64(int64_t nrows, int64_t ncols, int K, const int* offsets,
+                                 const float* vals, int64_t stride, const float* x, float* y,
+                                 int threads)
+{
+    (void)threads;
+#pragma omp parallel for schedule(static) num_threads(threads > 0 ? threads : 1)
+    for (int64_t i = 0; i < nrows; ++i) {
+        float sr = 0.0f, si = 0.0f;
+        for (int k = 0; k < K; ++k) {
+            const int64_t c = i + offsets[k];
+            if (c < 0 || c >= ncols) continue;
+            const float ar = vals[2 * ((size_t)k * stride + i)];
+            const float ai = vals[2 * ((size_t)k * stride + i) + 1];
+            const float xr = x[2 * c], xi = x[2 * c + 1];
+            const float p1 = ar * xr, p2 = ai * xi, p3 = ar * xi, p4 = ai * xr;
+            const float pr = p1 - p2, pi = p3 + p4;
+            sr = sr + pr;
+            si = si + pi;
+        }
+        y[2 * i] = sr;
+        y[2 * i + 1] = si;
+    }
+}
+
+/* exp(-i t A) x by the truncated Taylor series (dia_expm_taylor_c64):
+ * v_0 = x, v_j = (-i c_j) (A v_{j-1}) with c_j = fl(t/j), i.e.
+ * (re, im) = (fl(c_j * s_im), -fl(c_j * s_re)); y = y + v_j per element. */
+ORC_API void orc_expm_taylor_c64(int64_t n, int K, const int* offsets, const float* vals,
+                                 int64_t stride, float t, int m, const float* x, float* y,
+                                 int threads)
+{
+    float* v = (float*)malloc((size_t)n * 2 * sizeof(float));
+    float* w = (float*)malloc((size_t)n * 2 * sizeof(float));
+    memcpy(v, x, (size_t)n * 2 * sizeof(float));
+    memcpy(y, x, (size_t)n * 2 * sizeof(float));
+    for (int j = 1; j <= m; ++j) {
+        const float c = t / (float)j;
+        orc_spmv_rowidx_c64(n, n, K, offsets, vals, stride, v, w, threads);
+#pragma omp parallel for schedule(static) num_threads(threads > 0 ? threads : 1)
+        for (int64_t i = 0; i < n; ++i) {
+            const float re = c * w[2 * i + 1];
+            const float im = -(c * w[2 * i]);
+            w[2 * i] = re;
+            w[2 * i + 1] = im;
+            y[2 * i] = y[2 * i] + re;
+            y[2 * i + 1] = y[2 * i + 1] + im;
+        }
+        float* tmp = v;
+        v = w;
+        w = tmp;
+    }
+    free(v);
+    free(w);
+}
+
 /* ------------------------------------------------------------------------
  * SpMSpM symbolic phase
  * ------------------------------------------------------------------------ */

@@ -114,3 +114,29 @@ def test_expm_taylor_oracle_matches_matrix_exponential():
         assert np.linalg.norm(y - ref) / np.linalg.norm(ref) < 1e-6
     # m = 0 is the identity
     assert np.array_equal(oracle.expm_taylor(offs, vals, stride, 0.3, 0, x), x)
+
+
+def test_expm_taylor_c64_oracle_matches_matrix_exponential():
+    """exp(-i t H) x of a Hermitian band: the recurrence converges to scipy's
+    expm and keeps the norm (unitary evolution)."""
+    import scipy.linalg as sl
+    rng = np.random.default_rng(1)
+    n, stride = 80, 96
+    offs = np.array([-7, -1, 0, 1, 7], np.int32)
+    H = np.zeros((n, n), np.complex128)
+    for d in (0, 1, 7):
+        for i in range(n - d):
+            z = complex(rng.uniform(-1, 1), rng.uniform(-1, 1) if d else 0.0)
+            H[i, i + d] = z
+            H[i + d, i] = np.conj(z)
+    vals = np.zeros((len(offs), stride), np.complex64)
+    for k, d in enumerate(offs):
+        for i in range(max(0, -d), min(n, n - d)):
+            vals[k, i] = H[i, i + d]
+    x = (rng.uniform(-1, 1, n) + 1j * rng.uniform(-1, 1, n)).astype(np.complex64)
+    y = oracle.expm_taylor_c64(offs, vals, stride, 0.3, 20, x)
+    ref = sl.expm(-1j * 0.3 * H) @ x
+    assert np.linalg.norm(y - ref) / np.linalg.norm(ref) < 1e-6
+    assert abs(np.linalg.norm(y) / np.linalg.norm(x) - 1) < 1e-6
+    yv = oracle.spmv_c64(offs, vals, stride, x, n_rows=n, n_cols=n)
+    assert np.linalg.norm(yv - H @ x) / np.linalg.norm(H @ x) < 1e-6
