@@ -183,10 +183,16 @@ def nnz_rows(n, offs, r0, r1):
 
 
 def l2_flusher():
-    buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")  # 256 MB > L2
+    """Write a buffer larger than L2, then read another one: the write
+    evicts the timed kernel's data, and the read pass evicts the dirty lines
+    the write left, so their write-back happens here, outside the timed
+    bracket, instead of inside the next timed launch."""
+    wbuf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")  # 256 MB > L2
+    rbuf = torch.zeros(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
 
     def flush():
-        buf.zero_()
+        wbuf.zero_()
+        rbuf.sum()
     return flush
 
 
