@@ -238,5 +238,5 @@ extern "C" int dia_spmspm_rows_device(int64_t n, const int* d_A_off, const int* 
                                   d_nA, d_nC);
     if (rc) return rc;
     return launch_pair_sum(d_A_vals, d_B_vals, d_C_vals, w.outs, w.terms, nC_cap, 0, (int)n, false,
-                           stream, -1.0f, d_nC);
+                           stream, -1.0f, d_nC, 8);
 }

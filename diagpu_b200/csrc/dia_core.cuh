@@ -135,11 +135,13 @@ int persistent_blocks(const void* kernel, int smem_bytes);
 
 /* Persistent pair-sum kernel over nOut output diagonals and rows
  * [row_lo, row_hi) (spmspm.cu).  With nOut_dev the count is read on the
- * device and nOut is a capacity. */
+ * device and nOut is a capacity.  rows_per_thread is 4 or 8 (8 measured
+ * faster on matrix-power chain steps, 1.84 -> 1.55 ms for H^8 of the
+ * config-1 operator, and slower on the scattered config-3 product). */
 int launch_pair_sum(const float* U, const float* V, float* O, const OutDesc* outs,
                     const Term* terms, int nOut, int row_lo, int row_hi, bool accumulate,
                     cudaStream_t stream, float avg_terms = -1.0f,
-                    const int* nOut_dev = nullptr);
+                    const int* nOut_dev = nullptr, int rows_per_thread = 4);
 
 /* Term lists of a rows-layout product written into caller buffers (terms:
  * nC * nA slots, outs: nC), built on the device in A storage order

@@ -273,9 +273,13 @@ static int launch_pair_sum_t(const float* U, const float* V, float* O, const Out
  * rows [row_lo, row_hi). */
 int launch_pair_sum(const float* U, const float* V, float* O, const OutDesc* outs,
                     const Term* terms, int nOut, int row_lo, int row_hi, bool accumulate,
-                    cudaStream_t stream, float avg_terms, const int* nOut_dev)
+                    cudaStream_t stream, float avg_terms, const int* nOut_dev,
+                    int rows_per_thread)
 {
     if (nOut <= 0 || row_hi <= row_lo) return DIA_OK;
+    if (rows_per_thread == 8)
+        return launch_pair_sum_t<8, 4>(U, V, O, outs, terms, nOut, row_lo, row_hi, accumulate,
+                                       avg_terms, stream, nOut_dev);
     return launch_pair_sum_t<4, 4>(U, V, O, outs, terms, nOut, row_lo, row_hi, accumulate,
                                    avg_terms, stream, nOut_dev);
 }
