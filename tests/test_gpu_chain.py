@@ -131,3 +131,32 @@ def test_power_chain_has_no_host_sync():
     assert not ev.query()                 # nothing forced the host to wait
     torch.cuda.synchronize()
     assert chain.power().K == 61          # H^5: offsets 256a + b with |a| + |b| <= 5
+
+
+def test_symbolic_device_fuzz():
+    """Random sizes and offset sets, sums that fall outside (-n, n) included."""
+    rng = np.random.default_rng(2024)
+    for _ in range(40):
+        n = int(rng.integers(1, 3000))
+        na, nb = int(rng.integers(1, 40)), int(rng.integers(1, 12))
+        A = np.unique(rng.integers(-(n - 1), n, na)).astype(np.int32)
+        B = np.unique(rng.integers(-(n - 1), n, nb)).astype(np.int32)
+        ref = dg.spmspm_symbolic(n, A, B)["C_off"]
+        got, nc = _device_sumset(n, A, B, cap=len(A) * len(B) + 1, a_cap=len(A) + 5)
+        assert nc == len(ref) and np.array_equal(got[:nc], ref), (n, A, B)
+
+
+def test_power_chain_offsets_reach_the_matrix_edge():
+    """Powers whose sums leave (-n, n): those diagonals are dropped exactly as
+    the host symbolic phase drops them, values still equal the host path."""
+    n = 300
+    H = dg.DiaRows.synth(n, n, np.array([-120, -1, 0, 2, 150], np.int32), seed=8)
+    chain = dg.PowerChain(H, max_diags=200)
+    P = H
+    for _ in range(3):
+        chain.step()
+        P = dg.spmspm(P, H)
+        got = chain.power()
+        assert np.abs(got.offsets).max() < n
+        assert np.array_equal(got.offsets, P.offsets)
+        assert same(got.vals[:, :n].cpu().numpy(), P.vals[:, :n].cpu().numpy())

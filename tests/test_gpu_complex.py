@@ -78,3 +78,18 @@ def test_complex_entry_points_reject_real_values():
     A = dg.DiaRows.synth(64, 64, np.array([0], np.int32), seed=1)
     with pytest.raises(dg.DiaError):
         dg.spmv_c64(A, torch.zeros(64, dtype=torch.complex64, device="cuda"))
+
+
+@pytest.mark.parametrize("n_rows,n_cols", [(1000, 1700), (2048, 513)])
+def test_spmv_c64_rectangular(n_rows, n_cols):
+    rng = np.random.default_rng(n_rows + n_cols)
+    offs = np.array([-700, -2, 0, 3, 900], np.int32)
+    vals = rng.standard_normal((len(offs), n_rows)) + 1j * rng.standard_normal((len(offs), n_rows))
+    for k, d in enumerate(offs):
+        rows = np.arange(n_rows)
+        vals[k, (rows + d < 0) | (rows + d >= n_cols)] = 0
+    A = dg.DiaRows.from_host(n_rows, n_cols, offs, vals)
+    x = (rng.standard_normal(n_cols) + 1j * rng.standard_normal(n_cols)).astype(np.complex64)
+    y = dg.spmv_c64(A, torch.from_numpy(x).cuda()).cpu().numpy()
+    ref = oracle.spmv_c64(offs, A.vals.cpu().numpy(), A.stride, x, n_rows=n_rows, n_cols=n_cols)
+    assert same(y.view(np.float32), ref.view(np.float32))

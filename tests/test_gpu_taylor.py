@@ -53,3 +53,13 @@ def test_expm_taylor_rejects_partial_blocks():
     A = dg.DiaRows.synth(n, n, np.array([0], np.int32), seed=1, vrow0=64, nrows=64)
     with pytest.raises(dg.DiaError):
         dg.expm_taylor(A, 0.1, 3, torch.zeros(n, device="cuda"))
+
+
+def test_expm_taylor_negative_time_many_terms():
+    n = 3000
+    offs = np.array([-50, -1, 0, 1, 50], np.int32)
+    A = dg.DiaRows.synth(n, n, offs, seed=43)
+    x = dg.synth_vector(n, seed=44)
+    y = dg.expm_taylor(A, -0.2, 30, x)
+    ref = oracle.expm_taylor(offs, A.vals.cpu().numpy(), A.stride, -0.2, 30, x.cpu().numpy())
+    assert same(y.cpu().numpy(), ref)
