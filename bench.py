@@ -296,6 +296,14 @@ def single_gpu_extras(dg, steps, warmup, hbm, src):
                 "ms": round(ms, 4), "bytes": byts,
                 "roofline": roofline(byts / ms / 1e6, hbm, src),
                 "gpu_launches_per_step": TAYLOR_M})
+    # Lanczos (eigenvalues of the symmetric config-1 operator), all on the device
+    fn, byts = _only_lanczos(dg)
+    ms = timed(fn, max(3, steps // 10), min(warmup, 3))
+    out.append({"workload": f"config1 operator Lanczos, {LANCZOS_M} steps on the device "
+                            "(fused SpMV+dot, fp64 fixed-order reductions, no host sync)",
+                "metric": "lanczos_GBps", "value": round(byts / ms / 1e6, 1), "unit": "GB/s",
+                "ms": round(ms, 4), "bytes": byts, "roofline": roofline(byts / ms / 1e6, hbm, src),
+                "gpu_launches_per_step": 3 + 5 * LANCZOS_M})
     # complex64 SpMV (Hamiltonian-type operators), 27-point stencil on 256^3
     fn, byts = _only_spmv_c64(dg)
     ms = timed(fn, max(3, steps // 5), min(warmup, 3))
@@ -584,6 +592,21 @@ def _only_taylor(dg, n=1 << 20, m=TAYLOR_M):
     return (lambda: dg.expm_taylor(A, 0.01, m, x, y, work=work)), byts
 
 
+LANCZOS_M = 50
+
+
+def _only_lanczos(dg, n=1 << 20, m=LANCZOS_M):
+    """m Lanczos steps on the (symmetric) config-1 operator: per step a fused
+    SpMV + dot, an orthogonalisation + norm, a scaling, two tiny reductions."""
+    D = dg.DiaRows.empty(n, n, CHAIN_OFF)
+    for k, (d, b) in enumerate(zip(CHAIN_OFF, (-1.0, -1.0, 4.0, -1.0, -1.0))):
+        lo, hi = max(0, -int(d)), min(n, n - int(d))
+        D.vals[k, lo:hi] = b
+    x = dg.synth_vector(n, SEED_X)
+    byts = m * 4 * (nnz_rows(n, CHAIN_OFF, 0, n) + 8 * n)
+    return (lambda: dg.lanczos(D, m, x)), byts
+
+
 def _only_spmv_c64(dg, n=256 * 256 * 256):
     """complex64 SpMV, 27-point stencil offsets on a 256^3 grid (inputs > L2)."""
     A = dg.DiaRows.empty(n, n, OFF5, dtype=torch.complex64, zero=False)
@@ -631,6 +654,7 @@ ONLY = {
     "chain1": lambda dg: _only_chain(dg),
     "taylor1": lambda dg: _only_taylor(dg),
     "spmvc": lambda dg: _only_spmv_c64(dg),
+    "lanczos1": lambda dg: _only_lanczos(dg),
     "chain1_host": lambda dg: _only_chain(dg, host=True),
     "gemm4_simt": lambda dg: _only_gemm4(dg, mode=1),
 }

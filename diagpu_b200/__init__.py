@@ -84,6 +84,10 @@ def lib():
         L.dia_device_status.restype = i
         L.dia_synth_rows.argtypes = [u64, i64, i64, i, p, p, i, f, f, i64, i64, i64, p, p]
         L.dia_synth_vector.argtypes = [u64, i64, i64, f, f, p, p]
+        L.dia_lanczos_workspace.argtypes = [i64]
+        L.dia_lanczos_workspace.restype = i64
+        L.dia_lanczos.argtypes = [i64, i, p, p, i64, i, p, p, p, p, p, i64, p]
+        L.dia_lanczos.restype = i
         L.dia_spmv_rows_c64.argtypes = [i64, i64, i, p, p, i64, p, p, p]
         L.dia_expm_taylor_c64.argtypes = [i64, i, p, p, i64, f, i, p, p, p, p]
         for name in ("dia_spmv_rows_c64", "dia_expm_taylor_c64"):
@@ -291,6 +295,30 @@ def spmspm_hm(A_values, A_starts, A_off, A_len, B_values, B_starts, B_len, B_loo
                               _dptr(C_starts, torch.int64), _dptr(C_off, torch.int32),
                               _dptr(C_len, torch.int32), C_off.numel(), n, _stream(stream)))
     return C_values
+
+
+def lanczos(A: DiaRows, m, x, *, basis=False, stream=None):
+    """m Lanczos steps on a symmetric whole matrix (dia_lanczos), all on the
+    device.  Returns device fp64 tensors (alpha [m], beta [m]) of the
+    tridiagonal T_m, and with basis=True also the fp32 Lanczos vectors
+    [m, n]; eigenvalues of T_m (e.g. numpy.linalg.eigvalsh) approach A's
+    extreme eigenvalues.  Nothing synchronises with the host."""
+    if A.vrow0 != 0 or A.nrows != A.n_rows or A.n_rows != A.n_cols:
+        raise DiaError(DIA_ERR_INVALID, "lanczos: A must be a whole square matrix")
+    n = A.n_rows
+    dev = x.device
+    alpha = torch.zeros(max(m, 1), dtype=torch.float64, device=dev)
+    beta = torch.zeros(max(m, 1), dtype=torch.float64, device=dev)
+    B = torch.empty((max(m, 1), n), dtype=torch.float32, device=dev) if basis else None
+    L = lib()
+    ws = L.dia_lanczos_workspace(n)
+    work = torch.empty(max(ws, 1), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        check(L.dia_lanczos(n, A.K, _dptr(A.d_offsets), _dptr(A.vals), A.stride, int(m),
+                            _dptr(x, torch.float32), _dptr(alpha), _dptr(beta), _dptr(B),
+                            _dptr(work), ws, _stream(stream)))
+    out = (alpha[:m], beta[:m])
+    return out + (B[:m],) if basis else out
 
 
 def _whole_c64(A, who):

@@ -1,0 +1,201 @@
+/*
+ * krylov.cu -- Lanczos on a DIA operator, entirely on the device.
+ *
+ * For a symmetric A (a Hamiltonian, a Laplacian) m Lanczos steps build the
+ * tridiagonal T_m = tridiag(beta, alpha, beta) whose extreme eigenvalues
+ * approach A's (ground-state energies); together with the Taylor driver in
+ * spmv.cu this is the chain of SpMVs the reference's operators are built
+ * for -- the reference itself stops at single products.  One step j:
+ *     w      = fl(A v_j) - fl(beta_{j-1} * v_{j-1})      (SpMV fused, + alpha partials)
+ *     alpha_j = sum_i w_i * v_j,i                        (fp64, fixed-order tree)
+ *     w      = w - fl(alpha_j * v_j)                     (+ beta partials)
+ *     beta_j = sqrt(sum_i w_i^2)                         (fp64, fixed-order tree)
+ *     v_{j+1} = fl(w * fl(1 / beta_j))
+ * with alpha_j and beta_j kept in device memory (fp64) and used by the
+ * vector updates as fp32, so m steps run without any host synchronisation.
+ * Products of two fp32 values are exact in fp64, so the fp64 dot products
+ * agree with any other summation order to about 1e-16 relative; the fp32
+ * vector updates follow the order above, which the CPU oracle restates.
+ * The starting vector is normalised the same way (v_0 = x * fl(1/||x||)).
+ */
+#include <cmath>
+
+#include "../../include/diagpu_b200.h"
+#include "dia_core.cuh"
+
+namespace dia {
+
+constexpr int kKrThreads = 256;
+constexpr int kKrRows = kKrThreads * 4;   /* rows per CTA */
+
+/* fixed-order CTA reduction of one fp64 value per thread */
+__device__ __forceinline__ double block_sum(double v)
+{
+    __shared__ double s[kKrThreads / 32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) v += __shfl_down_sync(0xffffffffu, v, d);
+    if (lane == 0) s[warp] = v;
+    __syncthreads();
+    double t = 0.0;
+    if (threadIdx.x == 0)
+        for (int w = 0; w < kKrThreads / 32; ++w) t += s[w];
+    __syncthreads();
+    return t;   /* valid in thread 0 */
+}
+
+struct KrArgs {
+    const float* vals;
+    const int* off;
+    int K, n;
+    long long stride;
+};
+
+/* w = fl(A v) - fl(beta_prev * v_prev); part[b] = sum over the CTA's rows of w*v */
+__global__ void __launch_bounds__(kKrThreads)
+lanczos_spmv_kernel(KrArgs a, const float* __restrict__ v, const float* __restrict__ v_prev,
+                    const double* __restrict__ beta_prev, float* __restrict__ w,
+                    double* __restrict__ part)
+{
+    __shared__ int s_off[kMaxTerms];
+    const int K = min(a.K, kMaxTerms);
+    for (int k = threadIdx.x; k < K; k += kKrThreads) s_off[k] = a.off[k];
+    __syncthreads();
+    const float bp = beta_prev ? (float)*beta_prev : 0.0f;
+    double dot = 0.0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int i = blockIdx.x * kKrRows + j * kKrThreads + threadIdx.x;
+        if (i >= a.n) continue;
+        float s = 0.0f;
+        for (int k = 0; k < K; ++k) {
+            const int c = i + s_off[k];
+            if (c < 0 || c >= a.n) continue;
+            s = __fadd_rn(s, __fmul_rn(__ldcs(a.vals + (long long)k * a.stride + i), __ldg(v + c)));
+        }
+        const float wi = beta_prev ? __fsub_rn(s, __fmul_rn(bp, v_prev[i])) : s;
+        w[i] = wi;
+        dot += (double)wi * (double)v[i];
+    }
+    const double t = block_sum(dot);
+    if (threadIdx.x == 0) part[blockIdx.x] = t;
+}
+
+/* one CTA: out = sum of part[0..nb) in a fixed order, sqrt when asked */
+__global__ void __launch_bounds__(kKrThreads)
+lanczos_reduce_kernel(const double* __restrict__ part, int nb, double* __restrict__ out, int root)
+{
+    double acc = 0.0;
+    for (int b = threadIdx.x; b < nb; b += kKrThreads) acc += part[b];
+    const double t = block_sum(acc);
+    if (threadIdx.x == 0) *out = root ? sqrt(t) : t;
+}
+
+/* w = w - fl(alpha * v); part[b] = sum of w^2 */
+__global__ void __launch_bounds__(kKrThreads)
+lanczos_orth_kernel(int n, const float* __restrict__ v, const double* __restrict__ alpha,
+                    float* __restrict__ w, double* __restrict__ part)
+{
+    const float al = (float)*alpha;
+    double ss = 0.0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int i = blockIdx.x * kKrRows + j * kKrThreads + threadIdx.x;
+        if (i >= n) continue;
+        const float wi = __fsub_rn(w[i], __fmul_rn(al, v[i]));
+        w[i] = wi;
+        ss += (double)wi * (double)wi;
+    }
+    const double t = block_sum(ss);
+    if (threadIdx.x == 0) part[blockIdx.x] = t;
+}
+
+/* part[b] = sum of x^2 over the CTA's rows (x is only read) */
+__global__ void __launch_bounds__(kKrThreads)
+lanczos_norm_kernel(int n, const float* __restrict__ x, double* __restrict__ part)
+{
+    double ss = 0.0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int i = blockIdx.x * kKrRows + j * kKrThreads + threadIdx.x;
+        if (i < n) ss += (double)x[i] * (double)x[i];
+    }
+    const double t = block_sum(ss);
+    if (threadIdx.x == 0) part[blockIdx.x] = t;
+}
+
+/* v_next = fl(w * fl(1 / norm)) */
+__global__ void __launch_bounds__(kKrThreads)
+lanczos_scale_kernel(int n, const float* __restrict__ w, const double* __restrict__ norm,
+                     float* __restrict__ v_next)
+{
+    const float inv = __frcp_rn((float)*norm);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int i = blockIdx.x * kKrRows + j * kKrThreads + threadIdx.x;
+        if (i < n) v_next[i] = __fmul_rn(w[i], inv);
+    }
+}
+
+}  // namespace dia
+
+using namespace dia;
+
+extern "C" int64_t dia_lanczos_workspace(int64_t n)
+{
+    if (n <= 0) return -1;
+    const int64_t nb = (n + kKrRows - 1) / kKrRows;
+    return 4 * n * 4 + nb * 8 + 64;
+}
+
+extern "C" int dia_lanczos(int64_t n, int num_diags, const int* d_offsets, const float* d_vals,
+                           int64_t stride, int m, const float* d_x, double* d_alpha,
+                           double* d_beta, float* d_basis, void* d_work, int64_t work_bytes,
+                           cudaStream_t stream)
+{
+    if (n <= 0 || num_diags < 0 || m < 0 || stride < n)
+        return fail(DIA_ERR_INVALID, "dia_lanczos: bad sizes (stride must be >= n)");
+    if (num_diags > kMaxTerms)
+        return fail(DIA_ERR_UNSUPPORTED, "dia_lanczos: more diagonals than one CTA stages");
+    if (n + kKrRows >= (1LL << 31))
+        return fail(DIA_ERR_UNSUPPORTED, "dia_lanczos: n beyond int32 range");
+    if (!d_x || !d_alpha || !d_beta || !d_work || (num_diags > 0 && (!d_offsets || !d_vals)))
+        return fail(DIA_ERR_INVALID, "dia_lanczos: null pointer");
+    if (work_bytes < dia_lanczos_workspace(n))
+        return fail(DIA_ERR_INVALID, "dia_lanczos: workspace smaller than dia_lanczos_workspace()");
+    const int nb = (int)((n + kKrRows - 1) / kKrRows);
+    float* w = (float*)d_work;
+    float* vbuf[3] = {w + n, w + 2 * n, w + 3 * n};
+    double* part = (double*)(((uintptr_t)(w + 4 * n) + 7) & ~(uintptr_t)7);
+    double* norm0 = d_beta;   /* scratch for ||x|| before beta_0 is written */
+    /* v_0 = x * fl(1/||x||) */
+    lanczos_norm_kernel<<<nb, kKrThreads, 0, stream>>>((int)n, d_x, part);
+    DIA_TRY_CUDA(cudaGetLastError());
+    lanczos_reduce_kernel<<<1, kKrThreads, 0, stream>>>(part, nb, norm0, 1);
+    DIA_TRY_CUDA(cudaGetLastError());
+    lanczos_scale_kernel<<<nb, kKrThreads, 0, stream>>>((int)n, d_x, norm0, vbuf[0]);
+    DIA_TRY_CUDA(cudaGetLastError());
+    KrArgs a{d_vals, d_offsets, num_diags, (int)n, stride};
+    for (int j = 0; j < m; ++j) {
+        float* v = vbuf[j % 3];
+        float* vp = vbuf[(j + 2) % 3];
+        float* vn = vbuf[(j + 1) % 3];
+        if (d_basis)
+            DIA_TRY_CUDA(cudaMemcpyAsync(d_basis + (size_t)j * n, v, (size_t)n * 4,
+                                         cudaMemcpyDeviceToDevice, stream));
+        lanczos_spmv_kernel<<<nb, kKrThreads, 0, stream>>>(a, v, j ? vp : nullptr,
+                                                          j ? d_beta + j - 1 : nullptr, w, part);
+        DIA_TRY_CUDA(cudaGetLastError());
+        lanczos_reduce_kernel<<<1, kKrThreads, 0, stream>>>(part, nb, d_alpha + j, 0);
+        DIA_TRY_CUDA(cudaGetLastError());
+        lanczos_orth_kernel<<<nb, kKrThreads, 0, stream>>>((int)n, v, d_alpha + j, w, part);
+        DIA_TRY_CUDA(cudaGetLastError());
+        lanczos_reduce_kernel<<<1, kKrThreads, 0, stream>>>(part, nb, d_beta + j, 1);
+        DIA_TRY_CUDA(cudaGetLastError());
+        if (j + 1 < m) {
+            lanczos_scale_kernel<<<nb, kKrThreads, 0, stream>>>((int)n, w, d_beta + j, vn);
+            DIA_TRY_CUDA(cudaGetLastError());
+        }
+    }
+    return DIA_OK;
+}

@@ -165,6 +165,21 @@ int dia_spmspm_plan_execute(const DiaSpmspmPlan* plan, const float* d_A_vals,
                             int64_t row_hi, int use_tiles, cudaStream_t stream);
 int dia_spmspm_plan_destroy(DiaSpmspmPlan* plan);
 
+/* Lanczos on a symmetric DIA operator (whole matrix, rows layout, stride
+ * >= n), m steps without host synchronisation: d_alpha[0..m) and
+ * d_beta[0..max(m,1)) (fp64, device) receive the tridiagonal T_m whose
+ * extreme eigenvalues approach A's; d_basis (optional, m*n floats) receives
+ * v_0 .. v_{m-1}.  Per step: w = fl(A v_j) - fl(beta_{j-1} v_{j-1}),
+ * alpha_j = w.v_j and beta_j = ||w - fl(alpha_j v_j)|| in fp64 (exact
+ * products, fixed-order sums), v_{j+1} = fl(w * fl(1/beta_j)), scalars used
+ * as fp32 in the vector updates; v_0 = x * fl(1/||x||).  d_work holds
+ * dia_lanczos_workspace(n) bytes.  The reference has no eigensolver; this
+ * serves the ground-state energies of the operators it stores. */
+int64_t dia_lanczos_workspace(int64_t n);
+int dia_lanczos(int64_t n, int num_diags, const int* d_offsets, const float* d_vals,
+                int64_t stride, int m, const float* d_x, double* d_alpha, double* d_beta,
+                float* d_basis, void* d_work, int64_t work_bytes, cudaStream_t stream);
+
 /* Complex64 (interleaved fp32 re, im) DIA on the rows layout, whole matrix
  * (vrow0 = 0, stride in complex elements >= n_rows): y = A x with
  * per-term rounding re += fl(fl(ar*xr) - fl(ai*xi)), im += fl(fl(ar*xi) +

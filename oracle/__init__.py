@@ -42,6 +42,7 @@ def lib():
         L.orc_spmv_csr.argtypes = [i, _i32p, _i32p, _f32p, _f32p, _f32p]
         L.orc_spmv_rowidx.argtypes = [i64, i64, i64, i, _i32p, _f32p, i64, _f32p, i64, i64, _f32p, i]
         L.orc_expm_taylor.argtypes = [i64, i, _i32p, _f32p, i64, f, i, _f32p, _f32p, i]
+        L.orc_lanczos.argtypes = [i64, i, _i32p, _f32p, i64, i, _f32p, _f64p, _f64p, p]
         L.orc_spmv_rowidx_c64.argtypes = [i64, i64, i, _i32p, _f32p, i64, _f32p, _f32p, i]
         L.orc_expm_taylor_c64.argtypes = [i64, i, _i32p, _f32p, i64, f, i, _f32p, _f32p, i]
         L.orc_c_structure.argtypes = [i, _i32p, i, _i32p, i, p, p, p]
@@ -123,6 +124,17 @@ def expm_taylor(offsets, vals, stride, t, m, x, *, nthreads=None):
                           _a(vals, np.float32).reshape(-1), stride, float(t), int(m), x, y,
                           nthreads or threads())
     return y
+
+
+def lanczos(offsets, vals, stride, m, x, *, basis=False):
+    """(alpha, beta[, basis]) of m Lanczos steps by orc_lanczos."""
+    x = _a(x, np.float32)
+    al = np.zeros(max(m, 1), np.float64)
+    be = np.zeros(max(m, 1), np.float64)
+    B = np.zeros((max(m, 1), x.size), np.float32) if basis else None
+    lib().orc_lanczos(x.size, len(offsets), _a(offsets, np.int32), _a(vals, np.float32).reshape(-1),
+                      stride, int(m), x, al, be, B.ctypes.data_as(C.c_void_p) if basis else None)
+    return (al[:m], be[:m], B[:m]) if basis else (al[:m], be[:m])
 
 
 def _c64_as_f32(a):

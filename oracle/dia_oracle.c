@@ -18,6 +18,7 @@
  * (ref_*.cu shims) and tests/golden/make_golden.py records their outputs as
  * fixtures that tests/test_oracle.py replays against these functions.
  */
+#include <math.h>
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
@@ -156,6 +157,61 @@ ORC_API void orc_expm_taylor(int64_t n, int K, const int* offsets, const float* 
         w = tmp;
     }
     free(v);
+    free(w);
+}
+
+/* Lanczos on a symmetric DIA operator (the library's dia_lanczos): the
+ * reference has no eigensolver, so this is the definition the library
+ * follows.  fp32 vector updates in the order below, fp64 dot products of
+ * exact fp32 products (summed sequentially here; the library sums the same
+ * exact products in a fixed tree, agreeing to ~1e-16 relative), scalars
+ * rounded to fp32 where the vectors use them. */
+ORC_API void orc_lanczos(int64_t n, int K, const int* offsets, const float* vals, int64_t stride,
+                         int m, const float* x, double* alpha, double* beta, float* basis)
+{
+    float* v = (float*)malloc((size_t)n * sizeof(float));
+    float* vp = (float*)calloc((size_t)n, sizeof(float));
+    float* w = (float*)malloc((size_t)n * sizeof(float));
+    double ss = 0.0;
+    for (int64_t i = 0; i < n; ++i) ss += (double)x[i] * (double)x[i];
+    float inv = 1.0f / (float)sqrt(ss);
+    for (int64_t i = 0; i < n; ++i) v[i] = x[i] * inv;
+    for (int j = 0; j < m; ++j) {
+        if (basis) memcpy(basis + (size_t)j * n, v, (size_t)n * sizeof(float));
+        const float bp = j ? (float)beta[j - 1] : 0.0f;
+        double dot = 0.0;
+        for (int64_t i = 0; i < n; ++i) {
+            float s = 0.0f;
+            for (int k = 0; k < K; ++k) {
+                const int64_t c = i + offsets[k];
+                if (c < 0 || c >= n) continue;
+                const float p = vals[(size_t)k * stride + i] * v[c];
+                s = s + p;
+            }
+            if (j) {
+                const float q = bp * vp[i];
+                s = s - q;
+            }
+            w[i] = s;
+            dot += (double)s * (double)v[i];
+        }
+        alpha[j] = dot;
+        const float al = (float)dot;
+        ss = 0.0;
+        for (int64_t i = 0; i < n; ++i) {
+            const float q = al * v[i];
+            w[i] = w[i] - q;
+            ss += (double)w[i] * (double)w[i];
+        }
+        beta[j] = sqrt(ss);
+        inv = 1.0f / (float)beta[j];
+        float* t = vp;
+        vp = v;
+        v = t;
+        for (int64_t i = 0; i < n; ++i) v[i] = w[i] * inv;
+    }
+    free(v);
+    free(vp);
     free(w);
 }
 

@@ -140,3 +140,36 @@ def test_expm_taylor_c64_oracle_matches_matrix_exponential():
     assert abs(np.linalg.norm(y) / np.linalg.norm(x) - 1) < 1e-6
     yv = oracle.spmv_c64(offs, vals, stride, x, n_rows=n, n_cols=n)
     assert np.linalg.norm(yv - H @ x) / np.linalg.norm(H @ x) < 1e-6
+
+
+def _sym_band(g, seed):
+    """Rows-layout values of a symmetric 2D 5-point-type band on a g x g grid."""
+    n, stride = g * g, (g * g + 31) // 32 * 32
+    offs = np.array([-g, -1, 0, 1, g], np.int32)
+    rng = np.random.default_rng(seed)
+    vals = np.zeros((5, stride), np.float32)
+    for k, (d, b) in enumerate(zip(offs, (-1, -1, 4, -1, -1))):
+        lo, hi = max(0, -d), min(n, n - d)
+        vals[k, lo:hi] = b + rng.uniform(-0.01, 0.01, hi - lo)
+    for k, d in enumerate(offs):           # A[i, i+d] = A[i+d, i]
+        if d > 0:
+            vals[list(offs).index(-d), d:n] = vals[k, 0:n - d]
+    A = np.zeros((n, n))
+    for k, d in enumerate(offs):
+        i = np.arange(max(0, -d), min(n, n - d))
+        A[i, i + d] = vals[k, i]
+    return offs, vals, stride, A
+
+
+def test_lanczos_oracle_finds_extreme_eigenvalues():
+    """The Lanczos recurrence the library follows: its tridiagonal's extreme
+    eigenvalues converge to the operator's (numpy eigvalsh on the dense
+    matrix)."""
+    offs, vals, stride, A = _sym_band(20, 0)
+    assert np.array_equal(A, A.T)
+    x = np.random.default_rng(1).uniform(-1, 1, A.shape[0]).astype(np.float32)
+    al, be = oracle.lanczos(offs, vals, stride, 60, x)
+    T = np.diag(al) + np.diag(be[:-1], 1) + np.diag(be[:-1], -1)
+    ev, ea = np.linalg.eigvalsh(T), np.linalg.eigvalsh(A)
+    assert abs(ev.max() - ea.max()) / abs(ea.max()) < 1e-5
+    assert abs(ev.min() - ea.min()) / abs(ea.max()) < 1e-5
