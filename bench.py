@@ -182,6 +182,20 @@ def nnz_rows(n, offs, r0, r1):
     return sum(max(0, min(r1, n - int(d)) - max(r0, -int(d))) for d in offs)
 
 
+def tf32_peak_tflops(size=8192, reps=5):
+    """Dense TF32 throughput of this GPU (cuBLAS fp32 GEMM, TF32 allowed):
+    the denominator of gemm_diag's tensor-pipe fraction."""
+    a = torch.randn(size, size, device="cuda")
+    b = torch.randn(size, size, device="cuda")
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        ms = timed(lambda: a @ b, reps, 2)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    return 2 * size ** 3 / ms / 1e9
+
+
 def l2_flusher():
     """Write a buffer larger than L2, then read another one: the write
     evicts the timed kernel's data, and the read pass evicts the dirty lines
@@ -271,10 +285,20 @@ def single_gpu_extras(dg, steps, warmup, hbm, src):
     byts = 4 * (2 * nnz_rows(n, goff, 0, n) + tot)
     sym = dg.spmspm_symbolic(n, goff, goff)
     fl = spmspm_useful(n, goff, goff, sym, 0, n)
+    # TF32 peak of this GPU, measured: cuBLAS fp32 GEMM with TF32 tensor cores
+    tf32 = tf32_peak_tflops()
+    issued = 2 * 128 * 160 * 32 * ((n + 127) // 128) * 8   # 128x160x32 per chunk, 8 chunks a tile
     out.append({"workload": "config4 dense band hb=64 n=262144 gemm_diag (beta=0)",
                 "metric": "gemm_diag_useful_GFLOPs", "value": round(fl / ms / 1e6, 2),
                 "unit": "GFLOP/s", "ms": round(ms, 4), "bytes": byts, "useful_flops": fl,
-                "roofline": roofline(byts / ms / 1e6, hbm, src), "mode": "auto"})
+                "roofline": roofline(byts / ms / 1e6, hbm, src), "mode": "auto",
+                "tensor": {"tf32_peak_tflops_measured": round(tf32, 1),
+                           "useful_tflops": round(fl / ms / 1e9, 2),
+                           "issued_tflops": round(issued / ms / 1e9, 2),
+                           "frac_useful": round(fl / ms / 1e9 / tf32, 4),
+                           "frac_issued": round(issued / ms / 1e9 / tf32, 4),
+                           "note": "16 useful flop per algorithmic byte: HBM-bound far below "
+                                   "the TF32 ridge"}})
     del DA, DB, C
     # matrix-power chain H^8 of the config-1 operator, symbolic phase on the device
     fn, byts = _only_chain(dg)
