@@ -92,6 +92,8 @@ def lib():
         L.dia_expm_taylor_c64.argtypes = [i64, i, p, p, i64, f, i, p, p, p, p]
         for name in ("dia_spmv_rows_c64", "dia_expm_taylor_c64"):
             getattr(L, name).restype = i
+        L.dia_pauli_to_dia.argtypes = [i, i, p, p, p, p, p, p, p, i64, p]
+        L.dia_pauli_to_dia.restype = i
         L.dia_mtx_read.argtypes = [C.c_char_p, p, p, p, p, p, i64]
         L.dia_mtx_read.restype = i
         L.dia_expm_taylor.argtypes = [i64, i, p, p, i64, f, i, p, p, p, p]
@@ -354,6 +356,85 @@ def expm_taylor_c64(A: DiaRows, t, m, x, y=None, *, work=None, stream=None):
                                         _dptr(y, torch.complex64),
                                         _dptr(work, torch.complex64), _stream(stream)))
     return y
+
+
+def parse_pauli_sum(text):
+    """Terms of a Pauli-string sum in OpenFermion's QubitOperator text form,
+    e.g. "0.5 [X0 Y1] +\n(-0.25+0.1j) [Z2] +\n1.0 []"  ->  [(coef, "X0 Y1"), ...]."""
+    import re
+    terms = []
+    for m in re.finditer(r"([^\[\]]*)\[([^\]]*)\]", text):
+        coef = m.group(1).strip()
+        coef = re.sub(r"^\+", "", coef).strip()
+        coef = coef.replace(" ", "")
+        terms.append((complex(coef) if coef else 1.0, m.group(2).strip()))
+    return terms
+
+
+def _pauli_masks(terms, nq, big_endian):
+    xs, zs, cre, cim = [], [], [], []
+    top = 0
+    for coef, ops in terms:
+        x = z = 0
+        for op in ops.split():
+            p_, q = op[0].upper(), int(op[1:])
+            top = max(top, q + 1)
+            if nq is not None and q >= nq:
+                raise DiaError(DIA_ERR_INVALID, f"pauli_to_dia: qubit {q} >= nq = {nq}")
+            b = (nq - 1 - q) if big_endian else q
+            if p_ in "XY":
+                x |= 1 << b
+            if p_ in "ZY":
+                z |= 1 << b
+            if p_ not in "XYZI":
+                raise DiaError(DIA_ERR_INVALID, f"pauli_to_dia: unknown operator {op!r}")
+        xs.append(x)
+        zs.append(z)
+        c = complex(coef)
+        cre.append(c.real)
+        cim.append(c.imag)
+    return (np.array(xs, np.uint64), np.array(zs, np.uint64), np.array(cre, np.float64),
+            np.array(cim, np.float64), top)
+
+
+def pauli_to_dia_host(terms, nq=None, *, big_endian=False):
+    """H = sum_t c_t P_t (terms: [(coef, "X0 Y1 Z3"), ...] or QubitOperator
+    text) on the host (dia_pauli_to_dia).  Qubit k is bit k of the basis
+    index (big_endian=True: bit nq-1-k, OpenFermion's ordering).  Returns
+    (n, offsets int32 [K], vals complex64 [K, stride], is_real)."""
+    if isinstance(terms, str):
+        terms = parse_pauli_sum(terms)
+    if nq is None:
+        nq = max(1, _pauli_masks(terms, None, False)[4])
+    x, z, cre, cim, _ = _pauli_masks(terms, nq, big_endian)
+    L = lib()
+    pa = lambda a: a.ctypes.data_as(C.c_void_p)
+    K = C.c_int(0)
+    check(L.dia_pauli_to_dia(nq, len(terms), pa(x), pa(z), pa(cre), pa(cim), C.byref(K), None,
+                             None, 0, None))
+    n = 1 << nq
+    stride = round_stride(n)
+    offs = np.empty(max(K.value, 1), np.int32)
+    vals = np.empty((max(K.value, 1), stride), np.complex64)
+    real = C.c_int(0)
+    check(L.dia_pauli_to_dia(nq, len(terms), pa(x), pa(z), pa(cre), pa(cim), C.byref(K),
+                             pa(offs), pa(vals), stride, C.byref(real)))
+    return n, offs[:K.value], vals[:K.value], bool(real.value)
+
+
+def pauli_to_dia(terms, nq=None, *, big_endian=False, device="cuda", real="auto"):
+    """The Hamiltonian as a whole-matrix DiaRows: float32 when it is real
+    (real="auto") or real=True, else complex64 (for spmv_c64 /
+    expm_taylor_c64)."""
+    n, offs, vals, is_real = pauli_to_dia_host(terms, nq, big_endian=big_endian)
+    as_real = is_real if real == "auto" else bool(real)
+    if as_real and not is_real:
+        raise DiaError(DIA_ERR_INVALID, "pauli_to_dia: the operator has imaginary entries")
+    A = DiaRows.empty(n, n, offs, device=device,
+                      dtype=torch.float32 if as_real else torch.complex64)
+    if len(offs):
+        A.vals.copy_(torch.from_numpy(vals.real.copy() if as_real else vals))
+    return A
 
 
 def read_mtx_host(path):

@@ -1,0 +1,126 @@
+/*
+ * io_pauli.cu -- Pauli-string Hamiltonians into the DIA rows layout (host).
+ *
+ * The operators the reference's DIA format is built for (HamLib spin,
+ * QUBO and molecular Hamiltonians) are sums H = sum_t c_t P_t of Pauli
+ * strings on q qubits, n = 2^q.  In the symplectic form a string is two bit
+ * masks: x (qubits carrying X or Y) and z (qubits carrying Z or Y); with
+ * qubit k on bit k of the basis index (the convention of the reference's
+ * talk: an X or Y on qubit k moves the column by +-2^k),
+ *     P |c> = i^popcount(x & z) * (-1)^popcount(c & z) |c XOR x>,
+ * so row r of P has its single entry in column c = r XOR x, on diagonal
+ * d = c - r, and a string spans the 2^popcount(x) diagonals
+ * sum_k (+-2^k) over the bits k of x.  This file enumerates those
+ * offsets, then accumulates every term's entries row by row -- in double
+ * complex, terms in input order, one rounding to complex64 at the end --
+ * into vals[k*stride + r] (interleaved re, im).  is_real reports whether
+ * every imaginary part is exactly zero, so real operators can take the
+ * fp32 paths.  Two calls: sizes first (no value buffers), then the fill.
+ */
+#include <algorithm>
+#include <complex>
+#include <cstdint>
+#include <cstring>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/diagpu_b200.h"
+#include "dia_core.cuh"
+
+namespace {
+
+/* every offset sum_k s_k 2^k over the bits k of x, s_k = +1 or -1 */
+void string_offsets(uint64_t x, std::vector<int64_t>& out)
+{
+    std::vector<int64_t> acc{0};
+    for (int k = 0; k < 64; ++k) {
+        if (!((x >> k) & 1)) continue;
+        const int64_t w = (int64_t)1 << k;
+        std::vector<int64_t> next;
+        next.reserve(acc.size() * 2);
+        for (int64_t a : acc) {
+            next.push_back(a + w);
+            next.push_back(a - w);
+        }
+        acc.swap(next);
+    }
+    out.insert(out.end(), acc.begin(), acc.end());
+}
+
+}  // namespace
+
+using namespace dia;
+
+extern "C" int dia_pauli_to_dia(int nq, int nterms, const uint64_t* h_x_mask,
+                                const uint64_t* h_z_mask, const double* h_coef_re,
+                                const double* h_coef_im, int* num_diags, int* h_offsets,
+                                float* h_vals, int64_t stride, int* is_real)
+{
+    if (nq < 1 || nq > 30 || nterms < 0 || !num_diags)
+        return fail(DIA_ERR_INVALID, "dia_pauli_to_dia: need 1 <= nq <= 30 and num_diags");
+    if (nterms > 0 && (!h_x_mask || !h_z_mask || !h_coef_re))
+        return fail(DIA_ERR_INVALID, "dia_pauli_to_dia: null term arrays");
+    const int64_t n = (int64_t)1 << nq;
+    const uint64_t all = (uint64_t)n - 1;
+    for (int t = 0; t < nterms; ++t)
+        if ((h_x_mask[t] | h_z_mask[t]) & ~all)
+            return fail(DIA_ERR_INVALID, "dia_pauli_to_dia: a string acts on a qubit >= nq");
+    std::vector<int64_t> offs;
+    for (int t = 0; t < nterms; ++t) string_offsets(h_x_mask[t], offs);
+    std::sort(offs.begin(), offs.end());
+    offs.erase(std::unique(offs.begin(), offs.end()), offs.end());
+    if (offs.size() > ((size_t)1 << 16))
+        return fail(DIA_ERR_UNSUPPORTED, "dia_pauli_to_dia: more than 65536 diagonals (strings "
+                                         "with many X/Y are not banded; DIA does not suit them)");
+    const int K = (int)offs.size();
+    if (!h_offsets && !h_vals) {
+        *num_diags = K;
+        return DIA_OK;
+    }
+    if (*num_diags < K) {
+        *num_diags = K;
+        return fail(DIA_ERR_CAPACITY, "dia_pauli_to_dia: offset buffer smaller than the count");
+    }
+    *num_diags = K;
+    if (h_offsets)
+        for (int k = 0; k < K; ++k) h_offsets[k] = (int)offs[k];
+    if (!h_vals) return DIA_OK;
+    if (stride < n) return fail(DIA_ERR_INVALID, "dia_pauli_to_dia: stride smaller than 2^nq");
+    std::unordered_map<int64_t, int> idx;
+    for (int k = 0; k < K; ++k) idx[offs[k]] = k;
+    static const std::complex<double> ipow[4] = {{1, 0}, {0, 1}, {-1, 0}, {0, -1}};
+    std::vector<std::complex<double>> coef((size_t)nterms);
+    for (int t = 0; t < nterms; ++t)
+        coef[t] = std::complex<double>(h_coef_re[t], h_coef_im ? h_coef_im[t] : 0.0) *
+                  ipow[__builtin_popcountll(h_x_mask[t] & h_z_mask[t]) & 3];
+    for (int k = 0; k < K; ++k)
+        std::memset(h_vals + 2 * (size_t)k * (size_t)stride, 0,
+                    2 * (size_t)stride * sizeof(float));
+    /* rows in chunks, so the double accumulator stays K x chunk */
+    const int64_t chunk = std::min<int64_t>(n, (int64_t)1 << 16);
+    std::vector<std::complex<double>> acc((size_t)K * (size_t)chunk);
+    bool real = true;
+    for (int64_t r0 = 0; r0 < n; r0 += chunk) {
+        std::fill(acc.begin(), acc.end(), std::complex<double>(0.0, 0.0));
+        for (int t = 0; t < nterms; ++t) {
+            const uint64_t x = h_x_mask[t], z = h_z_mask[t];
+            for (int64_t r = r0; r < r0 + chunk; ++r) {
+                const uint64_t col = (uint64_t)r ^ x;
+                const int k = idx[(int64_t)col - r];
+                const double sign = (__builtin_popcountll(col & z) & 1) ? -1.0 : 1.0;
+                acc[(size_t)k * chunk + (size_t)(r - r0)] += sign * coef[t];
+            }
+        }
+        for (int k = 0; k < K; ++k) {
+            float* row = h_vals + 2 * (size_t)k * (size_t)stride;
+            for (int64_t r = r0; r < r0 + chunk; ++r) {
+                const std::complex<double> v = acc[(size_t)k * chunk + (size_t)(r - r0)];
+                row[2 * r] = (float)v.real();
+                row[2 * r + 1] = (float)v.imag();
+                real = real && row[2 * r + 1] == 0.0f;
+            }
+        }
+    }
+    if (is_real) *is_real = real ? 1 : 0;
+    return DIA_OK;
+}

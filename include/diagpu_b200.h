@@ -208,6 +208,22 @@ int dia_expm_taylor_c64(int64_t n, int num_diags, const int* d_offsets, const vo
 int dia_mtx_read(const char* path, int64_t* n_rows, int64_t* n_cols, int* num_diags,
                  int* h_offsets, float* h_vals, int64_t stride);
 
+/* Pauli-string Hamiltonians (the operators of HamLib's spin, QUBO and
+ * molecular sets) into the rows layout (host only, no GPU): H = sum_t c_t
+ * P_t on nq qubits (n = 2^nq rows), P_t in symplectic form -- x_mask = the
+ * qubits carrying X or Y, z_mask = those carrying Z or Y -- with qubit k on
+ * bit k of the basis index, so an X or Y on qubit k moves the column by
+ * +-2^k.  Writes the distinct offsets ascending and complex64 values
+ * (interleaved re, im; h_vals[2*(k*stride + r)]), summed in double
+ * complex in term order and rounded once; *is_real = 1 when every
+ * imaginary part is zero.  Two calls, as dia_mtx_read; coef_im may be
+ * NULL.  The reference reads HamLib files with tools outside its
+ * repository; the DIA mapping follows its talk's appendix
+ * (slides/transcript.md:97-116). */
+int dia_pauli_to_dia(int nq, int nterms, const uint64_t* h_x_mask, const uint64_t* h_z_mask,
+                     const double* h_coef_re, const double* h_coef_im, int* num_diags,
+                     int* h_offsets, float* h_vals, int64_t stride, int* is_real);
+
 /* Truncated Taylor series of exp(tA) x for a whole square matrix A on the
  * rows layout (stride >= n): v_0 = x, v_j = (t/j) * A v_{j-1}, y = sum of
  * v_0 .. v_m.  One fused kernel per term (SpMV, scale, running sum); d_work
