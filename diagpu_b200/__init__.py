@@ -95,6 +95,8 @@ def lib():
         L.dia_pauli_to_dia.argtypes = [i, i, p, p, p, p, p, p, p, i64, p]
         L.dia_pauli_to_dia.restype = i
         L.dia_mtx_read.argtypes = [C.c_char_p, p, p, p, p, p, i64]
+        L.dia_mtx_write.argtypes = [C.c_char_p, i64, i64, i, p, p, i64]
+        L.dia_mtx_write.restype = i
         L.dia_mtx_read.restype = i
         L.dia_expm_taylor.argtypes = [i64, i, p, p, i64, f, i, p, p, p, p]
         L.dia_expm_taylor.restype = i
@@ -452,6 +454,16 @@ def read_mtx_host(path):
                          offs.ctypes.data_as(C.c_void_p), vals.ctypes.data_as(C.c_void_p),
                          stride))
     return nr.value, nc.value, offs[:K.value], vals[:K.value]
+
+
+def write_mtx(path, n_rows, n_cols, offsets, vals):
+    """Write a host rows-layout matrix (offsets [K], vals float32 [K, stride])
+    as a Matrix Market coordinate file (dia_mtx_write)."""
+    offsets = np.ascontiguousarray(offsets, np.int32)
+    vals = np.ascontiguousarray(vals, np.float32)
+    check(lib().dia_mtx_write(os.fsencode(path), n_rows, n_cols, len(offsets),
+                              offsets.ctypes.data_as(C.c_void_p),
+                              vals.ctypes.data_as(C.c_void_p), vals.shape[1] if vals.ndim == 2 else 0))
 
 
 def read_mtx(path, *, device="cuda") -> DiaRows:

@@ -198,3 +198,42 @@ extern "C" int dia_mtx_read(const char* path, int64_t* n_rows, int64_t* n_cols, 
     g_cache = MtxEntries{};
     return DIA_OK;
 }
+
+/* The inverse: a rows-layout matrix (host buffers) written as a coordinate
+ * real general file, entries row by row with offsets ascending -- the order
+ * spmv/tools/gen_banded_mtx.cpp writes -- values with 9 significant digits
+ * (enough to read every fp32 value back exactly).  Entries outside the
+ * matrix are skipped; stored zeros are kept, so the file's structure is the
+ * DIA structure. */
+extern "C" int dia_mtx_write(const char* path, int64_t n_rows, int64_t n_cols, int num_diags,
+                             const int* h_offsets, const float* h_vals, int64_t stride)
+{
+    if (!path || n_rows < 0 || n_cols < 0 || num_diags < 0 || stride < n_rows ||
+        (num_diags > 0 && (!h_offsets || !h_vals)))
+        return fail(DIA_ERR_INVALID, "dia_mtx_write: bad arguments");
+    std::vector<int> order(num_diags);
+    for (int k = 0; k < num_diags; ++k) order[k] = k;
+    std::sort(order.begin(), order.end(),
+              [&](int a, int b) { return h_offsets[a] < h_offsets[b]; });
+    long long nnz = 0;
+    for (int k = 0; k < num_diags; ++k) {
+        const long long d = h_offsets[k];
+        const long long lo = std::max(0LL, -d), hi = std::min((long long)n_rows, n_cols - d);
+        if (hi > lo) nnz += hi - lo;
+    }
+    FILE* f = std::fopen(path, "w");
+    if (!f) return fail(DIA_ERR_INVALID, std::string("dia_mtx_write: cannot open ") + path);
+    std::fprintf(f, "%%%%MatrixMarket matrix coordinate real general\n");
+    std::fprintf(f, "%% written by diagpu_b200 from %d stored diagonals\n", num_diags);
+    std::fprintf(f, "%lld %lld %lld\n", (long long)n_rows, (long long)n_cols, nnz);
+    for (int64_t i = 0; i < n_rows; ++i)
+        for (int k : order) {
+            const int64_t c = i + h_offsets[k];
+            if (c < 0 || c >= n_cols) continue;
+            std::fprintf(f, "%lld %lld %.9g\n", (long long)(i + 1), (long long)(c + 1),
+                         (double)h_vals[(size_t)k * (size_t)stride + (size_t)i]);
+        }
+    const bool ok = std::ferror(f) == 0;
+    std::fclose(f);
+    return ok ? DIA_OK : fail(DIA_ERR_INVALID, "dia_mtx_write: write error");
+}

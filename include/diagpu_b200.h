@@ -207,6 +207,12 @@ int dia_expm_taylor_c64(int64_t n, int num_diags, const int* d_offsets, const vo
  * complex files. */
 int dia_mtx_read(const char* path, int64_t* n_rows, int64_t* n_cols, int* num_diags,
                  int* h_offsets, float* h_vals, int64_t stride);
+/* The inverse (host): the rows-layout matrix as a coordinate real general
+ * file, rows in order and offsets ascending within a row (the order of
+ * spmv/tools/gen_banded_mtx.cpp), 9 significant digits so every fp32 value
+ * reads back exactly; stored zeros inside the matrix are written too. */
+int dia_mtx_write(const char* path, int64_t n_rows, int64_t n_cols, int num_diags,
+                  const int* h_offsets, const float* h_vals, int64_t stride);
 
 /* Pauli-string Hamiltonians (the operators of HamLib's spin, QUBO and
  * molecular sets) into the rows layout (host only, no GPU): H = sum_t c_t
