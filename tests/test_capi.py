@@ -123,3 +123,21 @@ def test_validation_returns_status_not_exit():
                                 0, 1, 0, None) == dg.DIA_ERR_INVALID
     assert L.dia_dist_create(0, 0, None, C.byref(C.c_void_p())) == dg.DIA_ERR_INVALID
     assert L.dia_device_status(None, 0) == dg.DIA_ERR_INVALID
+
+
+def test_symbolic_fuzz_against_oracle():
+    """Random sizes and offset sets (storage order unsorted, sums leaving
+    (-n, n)): structure and pair lists equal the reference restatement."""
+    rng = np.random.default_rng(99)
+    for _ in range(60):
+        n = int(rng.integers(1, 5000))
+        A = rng.permutation(np.unique(rng.integers(-(n - 1), n, int(rng.integers(1, 30)))))
+        B = rng.permutation(np.unique(rng.integers(-(n - 1), n, int(rng.integers(1, 30)))))
+        A, B = A.astype(np.int32), B.astype(np.int32)
+        r = dg.spmspm_symbolic(n, A, B)
+        off, ln, st = oracle.c_structure(n, A, B)
+        assert np.array_equal(r["C_off"], off) and np.array_equal(r["C_len"], ln)
+        assert np.array_equal(r["C_start"], st)
+        ptr, pa, pb = oracle.pair_lists(n, A, B, off)
+        assert np.array_equal(r["pair_ptr"], ptr)
+        assert np.array_equal(r["pair_a"], pa) and np.array_equal(r["pair_b"], pb)
