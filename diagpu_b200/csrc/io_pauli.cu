@@ -96,19 +96,55 @@ extern "C" int dia_pauli_to_dia(int nq, int nterms, const uint64_t* h_x_mask,
     for (int k = 0; k < K; ++k)
         std::memset(h_vals + 2 * (size_t)k * (size_t)stride, 0,
                     2 * (size_t)stride * sizeof(float));
-    /* rows in chunks, so the double accumulator stays K x chunk */
-    const int64_t chunk = std::min<int64_t>(n, (int64_t)1 << 16);
+    /* Per term: the diagonal of row r depends only on the bits of r under x.
+     * Those bits, compressed to a pattern p (bit j of p = j-th set bit of
+     * x), come from four byte tables; kof[p] is the pattern's diagonal
+     * index.  No hashing per row. */
+    std::vector<uint32_t> byte_tab((size_t)nterms * 4 * 256);
+    std::vector<std::vector<int>> kof((size_t)nterms);
+    for (int t = 0; t < nterms; ++t) {
+        const uint64_t x = h_x_mask[t];
+        int bits[64], nb = 0;
+        for (int k = 0; k < 64; ++k)
+            if ((x >> k) & 1) bits[nb++] = k;
+        for (int byte = 0; byte < 4; ++byte)
+            for (int v = 0; v < 256; ++v) {
+                uint32_t pat = 0;
+                for (int j = 0; j < nb; ++j) {
+                    const int b = bits[j] - 8 * byte;
+                    if (b >= 0 && b < 8 && ((v >> b) & 1)) pat |= 1u << j;
+                }
+                byte_tab[((size_t)t * 4 + byte) * 256 + v] = pat;
+            }
+        kof[t].resize((size_t)1 << nb);
+        for (uint32_t pat = 0; pat < (1u << nb); ++pat) {
+            int64_t d = 0;   /* bit set in the row: column = row - 2^k, else + 2^k */
+            for (int j = 0; j < nb; ++j)
+                d += ((pat >> j) & 1) ? -((int64_t)1 << bits[j]) : ((int64_t)1 << bits[j]);
+            kof[t][pat] = idx[d];
+        }
+    }
+    /* rows in chunks, so the double accumulator (K x chunk) stays near 16 MB
+     * and in cache: a power of two between 256 rows and 2^16 */
+    int64_t chunk = 256;
+    while (chunk < ((int64_t)1 << 16) && (chunk * 2) * K * 16 <= ((int64_t)16 << 20)) chunk *= 2;
+    chunk = std::min<int64_t>(n, chunk);
     std::vector<std::complex<double>> acc((size_t)K * (size_t)chunk);
     bool real = true;
     for (int64_t r0 = 0; r0 < n; r0 += chunk) {
         std::fill(acc.begin(), acc.end(), std::complex<double>(0.0, 0.0));
         for (int t = 0; t < nterms; ++t) {
             const uint64_t x = h_x_mask[t], z = h_z_mask[t];
+            const uint32_t* tab = &byte_tab[(size_t)t * 4 * 256];
+            const int* kt = kof[t].data();
+            const std::complex<double> c = coef[t], mc = -coef[t];
             for (int64_t r = r0; r < r0 + chunk; ++r) {
                 const uint64_t col = (uint64_t)r ^ x;
-                const int k = idx[(int64_t)col - r];
-                const double sign = (__builtin_popcountll(col & z) & 1) ? -1.0 : 1.0;
-                acc[(size_t)k * chunk + (size_t)(r - r0)] += sign * coef[t];
+                const uint32_t ur = (uint32_t)r;
+                const uint32_t pat = tab[ur & 255] | tab[256 + ((ur >> 8) & 255)] |
+                                     tab[512 + ((ur >> 16) & 255)] | tab[768 + (ur >> 24)];
+                acc[(size_t)kt[pat] * chunk + (size_t)(r - r0)] +=
+                    __builtin_parityll(col & z) ? mc : c;
             }
         }
         for (int k = 0; k < K; ++k) {
