@@ -98,6 +98,8 @@ def lib():
         L.dia_mtx_write.argtypes = [C.c_char_p, i64, i64, i, p, p, i64]
         L.dia_mtx_write.restype = i
         L.dia_mtx_read.restype = i
+        L.dia_mtx_read_c64.argtypes = [C.c_char_p, p, p, p, p, p, i64, p]
+        L.dia_mtx_read_c64.restype = i
         L.dia_expm_taylor.argtypes = [i64, i, p, p, i64, f, i, p, p, p, p]
         L.dia_expm_taylor.restype = i
         L.dia_spmspm_device_workspace.argtypes = [i64, i, i, i]
@@ -456,6 +458,25 @@ def read_mtx_host(path):
     return nr.value, nc.value, offs[:K.value], vals[:K.value]
 
 
+def read_mtx_c64_host(path):
+    """Parse a Matrix Market coordinate file -- complex (general, symmetric,
+    skew-symmetric, hermitian) or real -- into complex64 rows on the host
+    (dia_mtx_read_c64).  Returns (n_rows, n_cols, offsets int32 [K], vals
+    complex64 [K, stride], is_complex)."""
+    L = lib()
+    bpath = os.fsencode(path)
+    nr, nc, K, cx = C.c_int64(0), C.c_int64(0), C.c_int(0), C.c_int(0)
+    check(L.dia_mtx_read_c64(bpath, C.byref(nr), C.byref(nc), C.byref(K), None, None, 0,
+                             C.byref(cx)))
+    offs = np.empty(max(K.value, 1), np.int32)
+    stride = round_stride(nr.value)
+    vals = np.empty((max(K.value, 1), stride), np.complex64)
+    check(L.dia_mtx_read_c64(bpath, C.byref(nr), C.byref(nc), C.byref(K),
+                             offs.ctypes.data_as(C.c_void_p), vals.ctypes.data_as(C.c_void_p),
+                             stride, C.byref(cx)))
+    return nr.value, nc.value, offs[:K.value], vals[:K.value], bool(cx.value)
+
+
 def write_mtx(path, n_rows, n_cols, offsets, vals):
     """Write a host rows-layout matrix (offsets [K], vals float32 [K, stride])
     as a Matrix Market coordinate file (dia_mtx_write)."""
@@ -470,6 +491,16 @@ def read_mtx(path, *, device="cuda") -> DiaRows:
     """A Matrix Market coordinate file as a whole-matrix DiaRows on the GPU."""
     n_rows, n_cols, offs, vals = read_mtx_host(path)
     A = DiaRows.empty(n_rows, n_cols, offs, device=device)
+    if len(offs):
+        A.vals.copy_(torch.from_numpy(vals))
+    return A
+
+
+def read_mtx_c64(path, *, device="cuda") -> DiaRows:
+    """A Matrix Market coordinate file as a complex64 whole-matrix DiaRows
+    on the GPU (for spmv_c64 / expm_taylor_c64)."""
+    n_rows, n_cols, offs, vals, _ = read_mtx_c64_host(path)
+    A = DiaRows.empty(n_rows, n_cols, offs, device=device, dtype=torch.complex64)
     if len(offs):
         A.vals.copy_(torch.from_numpy(vals))
     return A

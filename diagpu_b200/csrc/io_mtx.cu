@@ -9,8 +9,12 @@
  * zeros elsewhere.  Symmetric files mirror every off-diagonal entry,
  * skew-symmetric ones mirror it negated; duplicate coordinates are summed in
  * double precision in file order; pattern entries are 1.  Values are parsed
- * as double and rounded once to fp32.  Array (dense) and complex files are reported as
- * unsupported.
+ * as double and rounded once to fp32.  Array (dense) files are reported as
+ * unsupported.  Complex files (symmetry general, symmetric, skew-symmetric or
+ * hermitian; Hermitian mirrors the conjugate) are read by dia_mtx_read_c64
+ * into interleaved complex64 rows, which also accepts every real field
+ * (imaginary parts zero); dia_mtx_read refuses them rather than drop the
+ * imaginary parts.
  *
  * Two calls, like dia_spmspm_symbolic: the first (null outputs) parses the
  * file and returns the shape and the number of diagonals; the second fills
@@ -36,7 +40,8 @@ struct MtxEntries {
     std::string path;
     int64_t rows = 0, cols = 0;
     std::vector<int64_t> r, c;   /* 0-based, mirrored entries included */
-    std::vector<double> v;
+    std::vector<double> v, vi;   /* vi only for complex files */
+    bool complex = false;
 };
 
 thread_local MtxEntries g_cache;
@@ -73,15 +78,18 @@ int parse(const char* path, MtxEntries& e)
     if (!lower_eq(w[2], "coordinate"))
         return dia::fail(DIA_ERR_UNSUPPORTED, "dia_mtx_read: only coordinate files are supported");
     const bool pattern = lower_eq(w[3], "pattern");
-    if (!pattern && !lower_eq(w[3], "real") && !lower_eq(w[3], "double") &&
+    const bool cplx = lower_eq(w[3], "complex");
+    if (!pattern && !cplx && !lower_eq(w[3], "real") && !lower_eq(w[3], "double") &&
         !lower_eq(w[3], "integer"))
         return dia::fail(DIA_ERR_UNSUPPORTED,
                          std::string("dia_mtx_read: field '") + w[3] + "' is not supported");
-    int sym = 0;   /* 0 general, 1 symmetric, -1 skew-symmetric */
+    int sym = 0;   /* 0 general, 1 symmetric, -1 skew-symmetric, 2 hermitian */
     if (lower_eq(w[4], "symmetric"))
         sym = 1;
     else if (lower_eq(w[4], "skew-symmetric"))
         sym = -1;
+    else if (cplx && lower_eq(w[4], "hermitian"))
+        sym = 2;
     else if (!lower_eq(w[4], "general"))
         return dia::fail(DIA_ERR_UNSUPPORTED,
                          std::string("dia_mtx_read: symmetry '") + w[4] + "' is not supported");
@@ -100,6 +108,8 @@ int parse(const char* path, MtxEntries& e)
     e.path = path;
     e.rows = M;
     e.cols = N;
+    e.complex = cplx;
+    if (cplx) e.vi.reserve((size_t)L * (sym ? 2 : 1));
     e.r.reserve((size_t)L * (sym ? 2 : 1));
     e.c.reserve((size_t)L * (sym ? 2 : 1));
     e.v.reserve((size_t)L * (sym ? 2 : 1));
@@ -108,21 +118,30 @@ int parse(const char* path, MtxEntries& e)
         if (p >= end) return dia::fail(DIA_ERR_INVALID, "dia_mtx_read: fewer entries than declared");
         const long long i = std::strtoll(p, &q, 10);
         const long long j = std::strtoll(q, &q, 10);
-        double v = 1.0;
+        double v = 1.0, vi = 0.0;
         if (!pattern) {
             const char* vs = q;
             v = std::strtod(vs, &q);
             if (q == vs) return dia::fail(DIA_ERR_INVALID, "dia_mtx_read: entry without a value");
+        }
+        if (cplx) {
+            const char* vs = q;
+            vi = std::strtod(vs, &q);
+            if (q == vs)
+                return dia::fail(DIA_ERR_INVALID, "dia_mtx_read: complex entry without an "
+                                                  "imaginary part");
         }
         if (i < 1 || i > M || j < 1 || j > N)
             return dia::fail(DIA_ERR_INVALID, "dia_mtx_read: entry outside the matrix");
         e.r.push_back(i - 1);
         e.c.push_back(j - 1);
         e.v.push_back(v);
+        if (cplx) e.vi.push_back(vi);
         if (sym && i != j) {
             e.r.push_back(j - 1);
             e.c.push_back(i - 1);
             e.v.push_back(sym > 0 ? v : -v);
+            if (cplx) e.vi.push_back(sym == 1 ? vi : -vi);
         }
         p = q;
         next_line(p);
@@ -134,11 +153,14 @@ int parse(const char* path, MtxEntries& e)
 
 using namespace dia;
 
-extern "C" int dia_mtx_read(const char* path, int64_t* n_rows, int64_t* n_cols, int* num_diags,
-                            int* h_offsets, float* h_vals, int64_t stride)
+namespace {
+
+/* Shared body of the two readers; ncomp = 1 (fp32) or 2 (interleaved c64). */
+int read_into(const char* who, const char* path, int64_t* n_rows, int64_t* n_cols, int* num_diags,
+              int* h_offsets, float* h_vals, int64_t stride, int ncomp, int* is_complex)
 {
     if (!path || !n_rows || !n_cols || !num_diags)
-        return fail(DIA_ERR_INVALID, "dia_mtx_read: null pointer");
+        return fail(DIA_ERR_INVALID, std::string(who) + ": null pointer");
     MtxEntries& e = g_cache;
     if (e.path != path || (!h_offsets && !h_vals)) {
         const int rc = parse(path, e);
@@ -147,11 +169,18 @@ extern "C" int dia_mtx_read(const char* path, int64_t* n_rows, int64_t* n_cols, 
             return rc;
         }
     }
+    if (e.complex && ncomp == 1) {
+        g_cache = MtxEntries{};
+        return fail(DIA_ERR_UNSUPPORTED, std::string(who) + ": complex file; read it with "
+                                                            "dia_mtx_read_c64");
+    }
+    if (is_complex) *is_complex = e.complex ? 1 : 0;
     std::map<int64_t, int> diag;
     for (size_t t = 0; t < e.r.size(); ++t) diag.emplace(e.c[t] - e.r[t], 0);
     *n_rows = e.rows;
     *n_cols = e.cols;
-    if (diag.size() > (size_t)INT32_MAX) return fail(DIA_ERR_UNSUPPORTED, "dia_mtx_read: too many diagonals");
+    if (diag.size() > (size_t)INT32_MAX)
+        return fail(DIA_ERR_UNSUPPORTED, std::string(who) + ": too many diagonals");
     const int K = (int)diag.size();
     if (!h_offsets && !h_vals) {
         *num_diags = K;
@@ -159,10 +188,11 @@ extern "C" int dia_mtx_read(const char* path, int64_t* n_rows, int64_t* n_cols, 
     }
     if (*num_diags < K) {
         *num_diags = K;
-        return fail(DIA_ERR_CAPACITY, "dia_mtx_read: offset buffer smaller than the diagonal count");
+        return fail(DIA_ERR_CAPACITY, std::string(who) + ": offset buffer smaller than the "
+                                                         "diagonal count");
     }
     if (h_vals && stride < e.rows)
-        return fail(DIA_ERR_INVALID, "dia_mtx_read: stride smaller than the row count");
+        return fail(DIA_ERR_INVALID, std::string(who) + ": stride smaller than the row count");
     int k = 0;
     for (auto& kv : diag) {
         kv.second = k;
@@ -171,8 +201,8 @@ extern "C" int dia_mtx_read(const char* path, int64_t* n_rows, int64_t* n_cols, 
     }
     *num_diags = K;
     if (h_vals) {
-        for (int kk = 0; kk < K; ++kk)
-            std::memset(h_vals + (size_t)kk * (size_t)stride, 0, (size_t)stride * sizeof(float));
+        const size_t rowlen = (size_t)ncomp * (size_t)stride;
+        std::memset(h_vals, 0, (size_t)K * rowlen * sizeof(float));
         /* entries ordered by (diagonal, row), file order within a cell
          * (stable sort); a cell's duplicates are summed in double in that
          * order and rounded once */
@@ -187,16 +217,36 @@ extern "C" int dia_mtx_read(const char* path, int64_t* n_rows, int64_t* n_cols, 
         });
         for (size_t t = 0; t < idx.size();) {
             const size_t a = idx[t];
-            double s = 0.0;
+            double s = 0.0, si = 0.0;
             size_t u = t;
-            for (; u < idx.size() && kd[idx[u]] == kd[a] && e.r[idx[u]] == e.r[a]; ++u)
+            for (; u < idx.size() && kd[idx[u]] == kd[a] && e.r[idx[u]] == e.r[a]; ++u) {
                 s += e.v[idx[u]];
-            h_vals[(size_t)kd[a] * (size_t)stride + (size_t)e.r[a]] = (float)s;
+                if (e.complex) si += e.vi[idx[u]];
+            }
+            float* cell = h_vals + (size_t)kd[a] * rowlen + (size_t)ncomp * (size_t)e.r[a];
+            cell[0] = (float)s;
+            if (ncomp == 2) cell[1] = (float)si;
             t = u;
         }
     }
     g_cache = MtxEntries{};
     return DIA_OK;
+}
+
+}  // namespace
+
+extern "C" int dia_mtx_read(const char* path, int64_t* n_rows, int64_t* n_cols, int* num_diags,
+                            int* h_offsets, float* h_vals, int64_t stride)
+{
+    return read_into("dia_mtx_read", path, n_rows, n_cols, num_diags, h_offsets, h_vals, stride,
+                     1, nullptr);
+}
+
+extern "C" int dia_mtx_read_c64(const char* path, int64_t* n_rows, int64_t* n_cols, int* num_diags,
+                                int* h_offsets, float* h_vals, int64_t stride, int* is_complex)
+{
+    return read_into("dia_mtx_read_c64", path, n_rows, n_cols, num_diags, h_offsets, h_vals,
+                     stride, 2, is_complex);
 }
 
 /* The inverse: a rows-layout matrix (host buffers) written as a coordinate

@@ -203,10 +203,17 @@ int dia_expm_taylor_c64(int64_t n, int num_diags, const int* d_offsets, const vo
  * elsewhere (duplicates summed in double in file order, one rounding to
  * fp32).  Two calls: with h_offsets = h_vals = NULL it parses and returns
  * the shape and *num_diags; then with buffers (*num_diags = their capacity,
- * stride >= n_rows) it fills them.  DIA_ERR_UNSUPPORTED for array or
- * complex files. */
+ * stride >= n_rows) it fills them.  DIA_ERR_UNSUPPORTED for array files,
+ * and for complex files (read those with dia_mtx_read_c64). */
 int dia_mtx_read(const char* path, int64_t* n_rows, int64_t* n_cols, int* num_diags,
                  int* h_offsets, float* h_vals, int64_t stride);
+/* The same into interleaved complex64 rows (h_vals[2*(k*stride + i)] = re,
+ * [.. + 1] = im) for the c64 paths: complex files (general, symmetric,
+ * skew-symmetric, or hermitian -- mirrored entries conjugated) and every
+ * real field (imaginary parts zero).  *is_complex (may be NULL) = 1 when the
+ * file's field is complex. */
+int dia_mtx_read_c64(const char* path, int64_t* n_rows, int64_t* n_cols, int* num_diags,
+                     int* h_offsets, float* h_vals, int64_t stride, int* is_complex);
 /* The inverse (host): the rows-layout matrix as a coordinate real general
  * file, rows in order and offsets ascending within a row (the order of
  * spmv/tools/gen_banded_mtx.cpp), 9 significant digits so every fp32 value

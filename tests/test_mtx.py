@@ -85,7 +85,7 @@ def test_formats_match_scipy(tmp_path, case):
 def test_rejected_files(tmp_path, banner, code):
     path = str(tmp_path / "bad.mtx")
     with open(path, "w") as f:
-        f.write(banner + "\n2 2 1\n1 1 1.0\n")
+        f.write(banner + "\n2 2 1\n1 1 1.0 0.0\n")
     with pytest.raises(dg.DiaError) as e:
         dg.read_mtx_host(path)
     assert e.value.code == code
@@ -147,3 +147,60 @@ def test_write_reproduces_the_reference_generator_structure(tmp_path):
     body = lambda p: [ln.split()[:2] for ln in open(p) if not ln.startswith("%")][1:]
     assert body(out) == body(src)
     assert np.array_equal(_scipy_dense(out), _scipy_dense(src))
+
+
+def _dense_from_rows_c64(n_rows, n_cols, offs, vals):
+    A = np.zeros((n_rows, n_cols), np.complex64)
+    for k, d in enumerate(offs):
+        for i in range(n_rows):
+            j = i + int(d)
+            if 0 <= j < n_cols:
+                A[i, j] = vals[k, i]
+            else:
+                assert vals[k, i] == 0
+        assert (vals[k, n_rows:] == 0).all()
+    return A
+
+
+CASES_C64 = {
+    "complex general": ("complex general", 4, 5,
+                        [(1, 1, 1.5, -2.0), (2, 5, 0.25, 3.0), (4, 2, -1.0, 0.0), (1, 1, 0.5, 1.0)]),
+    "complex hermitian": ("complex hermitian", 4, 4,
+                          [(1, 1, 2.0, 0.0), (3, 1, 1.0, -0.5), (4, 2, -0.25, 2.0), (4, 4, 1.0, 0.0)]),
+    "complex symmetric": ("complex symmetric", 3, 3, [(2, 1, 1.0, 2.0), (3, 3, -1.0, 0.5)]),
+    "complex skew": ("complex skew-symmetric", 3, 3, [(3, 1, 0.5, -1.5)]),
+    "real as c64": ("real symmetric", 5, 5, [(1, 1, 2.5), (3, 1, -1.25), (5, 2, 0.5)]),
+}
+
+
+@pytest.mark.parametrize("case", sorted(CASES_C64))
+def test_c64_formats_match_scipy(tmp_path, case):
+    """dia_mtx_read_c64 against scipy.io.mmread, entry for entry (Hermitian
+    files mirror the conjugate, skew-symmetric the negation)."""
+    kind, m, n, entries = CASES_C64[case]
+    path = str(tmp_path / "c.mtx")
+    _write(path, kind, m, n, entries)
+    n_rows, n_cols, offs, vals, is_cx = dg.read_mtx_c64_host(path)
+    assert (n_rows, n_cols) == (m, n) and is_cx == kind.startswith("complex")
+    assert vals.dtype == np.complex64 and np.all(np.diff(offs) > 0)
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore")
+        ref = np.asarray(sio.mmread(path).toarray(), np.complex128).astype(np.complex64)
+    assert np.array_equal(_dense_from_rows_c64(n_rows, n_cols, offs, vals), ref)
+
+
+def test_c64_real_file_equals_fp32_reader():
+    path = os.path.join(GOLDEN, "banded_64.mtx")
+    _, _, offs, vals = dg.read_mtx_host(path)
+    _, _, o2, v2, is_cx = dg.read_mtx_c64_host(path)
+    assert not is_cx and np.array_equal(offs, o2)
+    assert np.array_equal(v2.real, vals) and not v2.imag.any()
+
+
+def test_c64_missing_imaginary_part(tmp_path):
+    path = str(tmp_path / "m.mtx")
+    with open(path, "w") as f:
+        f.write("%%MatrixMarket matrix coordinate complex general\n2 2 1\n1 1 1.0\n")
+    with pytest.raises(dg.DiaError) as e:
+        dg.read_mtx_c64_host(path)
+    assert e.value.code == dg.DIA_ERR_INVALID
