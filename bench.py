@@ -41,9 +41,9 @@ OFF5 = np.array([i + 256 * j + 65536 * k for k in (-1, 0, 1) for j in (-1, 0, 1)
                  for i in (-1, 0, 1)], np.int32)
 SEED_A, SEED_X = 5001, 5002
 REF_SAMPLE_ROWS = 4 * 1024 * 1024
-# DRAM bytes (read + write) of one spmv_kernel launch on config 5: the ncu
-# capture of the 4,194,304-row case (profiles/spmv_kernel_config5.md,
-# 471.4 MB) scaled by the ratio of algorithmic bytes (16.15)
+# DRAM bytes (read + write) of one spmv_kernel launch on config 5, derived
+# rather than measured by this run: the ncu capture of the 4,194,304-row case
+# (471.4 MB) scaled by the ratio of algorithmic bytes (16.15)
 SPMV5_TRAFFIC = 7_611_000_000
 
 
@@ -373,43 +373,114 @@ def setup_dist(args):
     return world, rank, local
 
 
+PARITY_W = 132 * 1024   # rows per parity window: covers every boundary tile (max|d| = 65,793)
+
+
+def spmv_window_ref(dg, w0, w1, x_full):
+    """Rows [w0, w1) of the whole-matrix y = A*x, computed by the 1-GPU
+    library path on a row window of A (equal to the oracle bit for bit,
+    tests/test_gpu_spmv.py)."""
+    Aw = dg.DiaRows.synth(N5, N5, OFF5, SEED_A, vrow0=w0, nrows=w1 - w0)
+    return dg.spmv(Aw, x_full)[:w1 - w0]
+
+
+def spmspm_window_ref(dg, w0, w1):
+    """Rows [w0, w1) of the whole-matrix C = A*A, from row windows of A
+    (rows [w0, w1)) and of B (the rows those need)."""
+    d = int(OFF5.max())
+    b0, b1 = max(0, w0 - d), min(N5, w1 + d)
+    Aw = dg.DiaRows.synth(N5, N5, OFF5, SEED_A, vrow0=w0, nrows=w1 - w0)
+    Bw = dg.DiaRows.synth(N5, N5, OFF5, SEED_A, vrow0=b0, nrows=b1 - b0)
+    plan = dg.SpmspmPlan(Aw, Bw)
+    Cw = plan.execute(Aw, Bw, plan.new_C())
+    return plan.C_off, Cw.vals[:, :w1 - w0]
+
+
+def parity_windows(r0, r1):
+    """Row windows checked on a rank: both block edges (every boundary tile
+    and the first interior tiles) and one window in the middle."""
+    w = min(PARITY_W, r1 - r0)
+    mid = (r0 + r1) // 2 // 1024 * 1024
+    out = {(r0, r0 + w), (r1 - w, r1), (mid, min(r1, mid + min(w, 16384)))}
+    return sorted(out)
+
+
+def all_ok(flag, world):
+    if world == 1:
+        return flag
+    t = torch.tensor([0 if flag else 1], device="cuda")
+    dist.all_reduce(t)
+    return int(t.item()) == 0
+
+
+def emit(line):
+    print(json.dumps(line, separators=(",", ":")), flush=True)
+
+
 def run_ours(args):
     import diagpu_b200 as dg
-    from diagpu_b200.dist import DistSpmspm, DistSpmv, Halo
+    from diagpu_b200.dist import PEER, DistSpmspm, DistSpmv, Halo
 
     world, rank, local = setup_dist(args)
     hbm, src = peaks()
     K, W = args.steps, args.warmup
+    clk = Clocks(list(range(world))) if rank == 0 else None
+    if clk is not None:
+        clk.__enter__()
     halo = Halo(N5, world, rank, int(OFF5.min()), int(OFF5.max()))
     r0, r1 = halo.r0, halo.r1
     A = dg.DiaRows.synth(N5, N5, OFF5, SEED_A, vrow0=r0, nrows=r1 - r0)
-    ds = DistSpmv(A, halo)
+    ds = DistSpmv(A, halo)   # world > 1: the fused peer-halo step kernel
     dg.synth_vector(r1 - r0, SEED_X, i0=r0, out=ds.x_own)
     launches = []
     ds.step(launches)
     per_step = len(launches)
     torch.cuda.synchronize()
 
-    # headline: K full steps (halo exchange + interior + boundary)
+    # headline: K full steps (halo exchange + every row of the block)
     for _ in range(W):
         ds.step()
     barrier(world)
-    with Clocks(list(range(world))) as clk:
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        for _ in range(K):
-            ds.step()
-        e.record()
-        e.synchronize()
-        barrier(world)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(K):
+        ds.step()
+    e.record()
+    e.synchronize()
+    barrier(world)
     ms = max_over_ranks(s.elapsed_time(e) / K, world)
     total_bytes, nnz = spmv_bytes(N5, OFF5, 0, N5)
     value = total_bytes / ms / 1e6
+    peer_status = ds.native.status() if ds.native is not None else 0
 
-    # dominant kernel alone (this rank's whole block, no exchange)
+    # breakdown of one step: this rank's block kernel alone with no exchange
+    # (back to back, and bracketed per launch for the roofline), and at N > 1
+    # the NCCL forms it replaces (halo alone; halo + interior + strips)
     rank_bytes, _ = spmv_bytes(N5, OFF5, r0, r1)
-    kms = timed(lambda: dg.spmv(A, ds.x_ext, ds.y, x_lo=halo.xlo), K, W, per_launch=True)
-    kms = max_over_ranks(kms, world)
+    kern = lambda: dg.spmv(A, ds.x_ext, ds.y, x_lo=halo.xlo)
+    kms_b2b = max_over_ranks(timed(kern, K, W, world=world), world)
+    kms = max_over_ranks(timed(kern, K, W, per_launch=True), world)
+    breakdown = {"step_ms": round(ms, 5), "kernel_alone_ms": round(kms_b2b, 5),
+                 "kernel_alone_per_launch_ms": round(kms, 5),
+                 "step_minus_kernel_ms": round(ms - kms_b2b, 5),
+                 "exchange": "fused peer push (NVLink stores + step flag) inside the step kernel"
+                 if world > 1 else "none (1 GPU)"}
+    if world > 1:
+        from diagpu_b200 import _stream, check, lib
+        ds2 = DistSpmv(A, halo, native=ds.native, overlap=2)
+        ds2.x_ext.copy_(ds.x_ext)
+        breakdown["nccl_overlap_step_ms"] = round(
+            max_over_ranks(timed(lambda: ds2.step(), K, W, world=world), world), 5)
+        rg = ds.native._ranges if hasattr(ds.native, "_ranges") else halo.ranges()
+        import ctypes as C
+
+        def halo_only():
+            check(lib().dia_dist_halo_start(ds.native.handle, dg._dptr(ds2.x_ext), halo.xlo, 0,
+                                            1, rg.ctypes.data_as(C.c_void_p), _stream()))
+            check(lib().dia_dist_halo_wait(ds.native.handle, _stream()))
+        breakdown["nccl_halo_alone_ms"] = round(
+            max_over_ranks(timed(halo_only, K, W, world=world), world), 5)
+        del ds2
 
     # end to end through the public API: every step copies its x from pinned
     # host memory and its y back.  Steps are pipelined as a streaming user
@@ -458,9 +529,23 @@ def run_ours(args):
     e2.record()
     e2.synchronize()
     ems = max_over_ranks(s2.elapsed_time(e2) / K, world)
-    assert torch.equal(yh, ds.y[:n_own].cpu()), "e2e result differs from the device result"
+    e2e_same = bool(torch.equal(yh, ds.y[:n_own].cpu()))
+    peer_status |= ds.native.status() if ds.native is not None else 0
+
+    # parity of the partitioned SpMV: this rank's rows on windows at both
+    # block edges and in the middle against the whole-matrix product
+    x_full = dg.synth_vector(N5, SEED_X)
+    wins = parity_windows(r0, r1)
+    ok_spmv = e2e_same and peer_status == 0
+    for w0, w1 in wins:
+        ok_spmv &= bool(torch.equal(ds.y[w0 - r0:w1 - r0], spmv_window_ref(dg, w0, w1, x_full)))
+    ok_spmv = all_ok(ok_spmv, world)
+    del x_full
+    torch.cuda.empty_cache()
 
     # secondary: C = A*A on the same partitioned matrix
+    if ds.native is not None:
+        ds.native = None
     del ds
     B_ext = dg.DiaRows.empty(N5, N5, OFF5, vrow0=halo.xlo, nrows=halo.width, zero=True)
     B_ext.vals[:, r0 - halo.xlo:r1 - halo.xlo] = A.vals[:, :r1 - r0]
@@ -472,45 +557,67 @@ def run_ours(args):
     nnzC = int(sym["C_len"].astype(np.int64).sum())
     mm_bytes = 4 * (nnz + nnzC)
     rank_mm_bytes = 4 * (nnz_rows(N5, OFF5, r0, r1) + nnz_rows(N5, sym["C_off"], r0, r1))
-    secondary = [{
-        "workload": "config5 C=A*A (125 output diagonals, 729 pairs)",
-        "metric": "spmspm_useful_GFLOPs", "value": round(fl / mm_ms / 1e6, 2), "unit": "GFLOP/s",
-        "ms": round(mm_ms, 4), "bytes": mm_bytes, "useful_flops": fl,
-        "GBps": round(mm_bytes / mm_ms / 1e6, 1),
-        "roofline": roofline(rank_mm_bytes / mm_ms / 1e6, hbm, src)}]
-    del dm, B_ext, A
+    del B_ext
+    torch.cuda.empty_cache()
+    ok_mm = True
+    for w0, w1 in wins:
+        c_off, Cw = spmspm_window_ref(dg, w0, w1)
+        ok_mm &= bool(np.array_equal(c_off, dm.C.offsets)) and bool(
+            torch.equal(dm.C.vals[:, w0 - r0:w1 - r0], Cw))
+        del Cw
+    ok_mm = all_ok(ok_mm, world)
+    spmspm5 = {"workload": "config5 C=A*A (125 output diagonals, 729 pairs)",
+               "metric": "spmspm_useful_GFLOPs", "value": round(fl / mm_ms / 1e6, 2),
+               "unit": "GFLOP/s", "ms": round(mm_ms, 4), "GBps": round(mm_bytes / mm_ms / 1e6, 1),
+               "bytes": mm_bytes, "useful_flops": fl, "n_gpus": world,
+               "roofline": roofline(rank_mm_bytes / mm_ms / 1e6, hbm, src)}
+    del dm, A
     torch.cuda.empty_cache()
 
+    extras = []
     cpu = None
     if world == 1:
-        secondary += single_gpu_extras(dg, K, W, hbm, src)
+        extras = single_gpu_extras(dg, K, W, hbm, src)
         if not args.no_cpu_baseline:
             cpu = cpu_port_baseline()
+    clocks = None
+    if clk is not None:
+        clk.__exit__(None, None, None)
+        clocks = clk.summary()
 
     if rank == 0:
-        line = {
+        for x in extras + [spmspm5]:
+            emit({"secondary": x})
+        rl = roofline(rank_bytes / kms / 1e6, hbm, src,
+                      traffic=SPMV5_TRAFFIC if world == 1 else None)
+        if world == 1:
+            rl["traffic_source"] = "ncu capture of the 4,194,304-row case, scaled to a full launch"
+        emit({
             "metric": "spmv_GBps", "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
             "steps": K, "warmup": W, "ms_per_step": round(ms, 5), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic: counter-hash uniform[-1,1] values, seeded, generated on device",
             "config": {"workload": "config5 DIA SpMV y=A*x, 3D 27-point stencil 256x256x1024",
                        "n": N5, "diagonals": 27, "nnz": nnz, "bytes_per_step": total_bytes,
-                       "parallelism": f"row-block x{world}, NCCL x halo +-65793",
+                       "parallelism": f"row-block x{world}, x halo +-65793 pushed over NVLink "
+                                      "by the step kernel" if world > 1 else "1 GPU",
                        "l2": "inputs 7.8 GB > 126 MB L2 (no flush needed)"},
-            "roofline": roofline(rank_bytes / kms / 1e6, hbm, src,
-                                 traffic=SPMV5_TRAFFIC if world == 1 else None),
-            "kernel_ms": round(kms, 5),
+            "roofline": rl, "kernel_ms": round(kms, 5), "breakdown": breakdown,
+            "parity": {"spmv": "bitexact" if ok_spmv else "MISMATCH",
+                       "spmspm": "bitexact" if ok_mm else "MISMATCH",
+                       "against": "1-GPU library product of the whole matrix on row windows",
+                       "windows_per_rank": len(wins), "window_rows": PARITY_W},
+            "spmspm5": {"ms": spmspm5["ms"], "GFLOPs": spmspm5["value"],
+                        "frac": spmspm5["roofline"]["frac"]},
             "cpu_baseline": cpu,
             "e2e": {"value": round(total_bytes / ems / 1e6, 1), "unit": "GB/s",
                     "ms_per_step": round(ems, 4),
                     "h2d_bytes_per_step": 4 * N5, "d2h_bytes_per_step": 4 * N5,
-                    "api": "diagpu_b200.dist.DistSpmv.step (dia_spmv_rows), pinned host x/y, "
-                           "steps pipelined (H2D, SpMV, D2H on three streams)"},
-            "clocks": clk.summary(),
+                    "api": "diagpu_b200.dist.DistSpmv.step, pinned host x/y, steps pipelined "
+                           "(H2D, SpMV, D2H on three streams)"},
+            "clocks": clocks,
             "gpu_launches": per_step * K,
-            "secondary": secondary,
-        }
-        print(json.dumps(line), flush=True)
+        })
     if world > 1:
         dist.destroy_process_group()
 

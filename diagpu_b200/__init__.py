@@ -76,9 +76,16 @@ def lib():
                                          i64, i64, i64, i, p]
         L.dia_dist_async_error.argtypes = [p]
         L.dia_dist_destroy.argtypes = [p]
+        L.dia_spmv_rows_peer.argtypes = [p, u64, i64, i64, i, p, p, i64, i64, i64, i64, i64, i64,
+                                         i, i, p, p, p]
+        L.dia_dist_peer_setup.argtypes = [p, i64, i64, i64, i64, p]
+        L.dia_dist_spmv_fused.argtypes = [p, i64, i64, i, p, p, i64, i64, i, i, p, p, p]
+        L.dia_dist_set_timeout.argtypes = [p, i64]
+        L.dia_dist_status.argtypes = [p, p, i]
         for name in ("dia_nccl_unique_id", "dia_dist_create", "dia_dist_halo_start",
                      "dia_dist_halo_wait", "dia_dist_spmv_step", "dia_dist_async_error",
-                     "dia_dist_destroy"):
+                     "dia_dist_destroy", "dia_spmv_rows_peer", "dia_dist_peer_setup",
+                     "dia_dist_spmv_fused", "dia_dist_set_timeout", "dia_dist_status"):
             getattr(L, name).restype = i
         L.dia_device_status.argtypes = [p, i]
         L.dia_device_status.restype = i

@@ -12,7 +12,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libdiagpu_b200.so")
 SOURCES = ["status.cu", "spmv.cu", "spmspm.cu", "spmspm_tiled.cu", "spmspm_runpair.cu", "symbolic.cu", "gemm_diag.cu",
-           "gemm_diag_tc.cu", "synth.cu", "dist.cu", "chain.cu", "io_mtx.cu", "krylov.cu", "io_pauli.cu"]
+           "gemm_diag_tc.cu", "synth.cu", "dist.cu", "dist_peer.cu", "chain.cu", "io_mtx.cu", "krylov.cu", "io_pauli.cu"]
 NVCC = os.environ.get("NVCC", "nvcc")
 FLAGS = ["-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo",
          "-Xcompiler", "-fPIC", "-Xptxas", "-O3", "--expt-relaxed-constexpr",

@@ -24,6 +24,7 @@
 
 #include <cstring>
 #include <string>
+#include <vector>
 
 #include "../../include/diagpu_b200.h"
 #include "dia_core.cuh"
@@ -33,6 +34,13 @@ struct DiaDist {
     cudaStream_t cs = nullptr;
     cudaEvent_t ready = nullptr, done = nullptr;
     int rank = 0, world = 1;
+    /* peer-memory halo (dia_dist_peer_setup) */
+    void* window = nullptr;        /* this rank's receive window */
+    void* peer_win[2] = {nullptr, nullptr}; /* IPC mappings of left / right windows */
+    DiaPeerHalo ph{};
+    uint64_t step = 0;
+    int64_t r0 = 0, r1 = 0, x_lo = 0, x_hi = 0;
+    bool peer_ready = false;
 };
 
 namespace {
@@ -215,10 +223,174 @@ extern "C" int dia_dist_destroy(DiaDist* d)
 {
     if (!d) return DIA_OK;
     if (d->cs) cudaStreamSynchronize(d->cs);
+    if (d->window) {
+        /* every step kernel of this rank has finished, and each of them
+         * waited for both neighbours' last pushes into this window */
+        cudaDeviceSynchronize();
+        for (void* p : d->peer_win)
+            if (p) cudaIpcCloseMemHandle(p);
+        cudaFree(d->window);
+    }
     if (d->comm) ncclCommDestroy(d->comm);
     if (d->ready) cudaEventDestroy(d->ready);
     if (d->done) cudaEventDestroy(d->done);
     if (d->cs) cudaStreamDestroy(d->cs);
     delete d;
+    return DIA_OK;
+}
+
+/* ------------------------------------------------------ peer-memory halo */
+
+namespace {
+
+/* Receive window layout: a 256-byte control block (flag_lo, flag_hi,
+ * push_count[2], status), then halo_lo[2] and halo_hi[2], each rounded up to
+ * 64 floats. */
+struct WinLayout {
+    size_t lo_off[2], hi_off[2], bytes;
+};
+
+WinLayout win_layout(int64_t lo_len, int64_t hi_len)
+{
+    auto r64 = [](int64_t v) { return (size_t)((v + 63) / 64 * 64) * sizeof(float); };
+    WinLayout w{};
+    size_t o = 256;
+    for (int p = 0; p < 2; ++p) { w.lo_off[p] = o; o += r64(lo_len); }
+    for (int p = 0; p < 2; ++p) { w.hi_off[p] = o; o += r64(hi_len); }
+    w.bytes = o;
+    return w;
+}
+
+struct PeerInfo {
+    cudaIpcMemHandle_t handle;
+    int64_t lo_len, hi_len;
+    int64_t valid;
+};
+
+}  // namespace
+
+extern "C" int dia_dist_peer_setup(DiaDist* d, int64_t r0, int64_t r1, int64_t x_lo, int64_t x_hi,
+                                   const int64_t* rg)
+{
+    if (!d || !rg) return fail(DIA_ERR_INVALID, "dia_dist_peer_setup: null pointer");
+    if (d->window) return fail(DIA_ERR_INVALID, "dia_dist_peer_setup: already set up");
+    if (x_lo > r0 || x_hi < r1 || r1 < r0)
+        return fail(DIA_ERR_INVALID, "dia_dist_peer_setup: inconsistent halo window");
+    const int64_t lo_len = r0 - x_lo, hi_len = x_hi - r1;
+    const WinLayout w = win_layout(lo_len, hi_len);
+    DIA_TRY_CUDA(cudaMalloc(&d->window, w.bytes));
+    DIA_TRY_CUDA(cudaMemset(d->window, 0, w.bytes));
+    PeerInfo mine{};
+    cudaError_t e = cudaIpcGetMemHandle(&mine.handle, d->window);
+    mine.valid = e == cudaSuccess;
+    mine.lo_len = lo_len;
+    mine.hi_len = hi_len;
+    /* every rank takes part in the exchange even when its handle failed, so
+     * that all ranks see the failure instead of hanging in the collective */
+    PeerInfo* dbuf = nullptr;
+    DIA_TRY_CUDA(cudaMalloc(&dbuf, sizeof(PeerInfo) * (size_t)(d->world + 1)));
+    DIA_TRY_CUDA(cudaMemcpy(dbuf + d->world, &mine, sizeof(mine), cudaMemcpyHostToDevice));
+    ncclResult_t nr = ncclAllGather(dbuf + d->world, dbuf, sizeof(PeerInfo), ncclChar, d->comm,
+                                    d->cs);
+    std::vector<PeerInfo> all((size_t)d->world);
+    if (nr == ncclSuccess) e = cudaStreamSynchronize(d->cs);
+    if (nr == ncclSuccess && e == cudaSuccess)
+        e = cudaMemcpy(all.data(), dbuf, sizeof(PeerInfo) * (size_t)d->world,
+                       cudaMemcpyDeviceToHost);
+    cudaFree(dbuf);
+    if (nr != ncclSuccess) return nccl_fail(nr, "dia_dist_peer_setup: ncclAllGather");
+    if (e != cudaSuccess) return cuda_fail(e, "dia_dist_peer_setup: handle exchange");
+    for (const PeerInfo& pi : all)
+        if (!pi.valid)
+            return fail(DIA_ERR_UNSUPPORTED,
+                        "dia_dist_peer_setup: cudaIpcGetMemHandle failed on some rank");
+    DiaPeerHalo& h = d->ph;
+    h = DiaPeerHalo{};
+    char* base = (char*)d->window;
+    auto* ctl = (unsigned long long*)base;
+    h.flag_lo = ctl + 0;
+    h.flag_hi = ctl + 1;
+    h.push_count = ctl + 2;
+    h.status = (unsigned int*)(ctl + 4);
+    for (int p = 0; p < 2; ++p) {
+        h.halo_lo[p] = lo_len ? (float*)(base + w.lo_off[p]) : nullptr;
+        h.halo_hi[p] = hi_len ? (float*)(base + w.hi_off[p]) : nullptr;
+    }
+    h.timeout_ns = 2000000000LL;
+    h.send_left_hi = r0;
+    h.send_right_lo = r1;
+    for (int side = 0; side < 2; ++side) {
+        const int peer = side == 0 ? d->rank - 1 : d->rank + 1;
+        if (peer < 0 || peer >= d->world) continue;
+        const PeerInfo& pi = all[(size_t)peer];
+        /* what this rank sends must be what the neighbour expects */
+        const int64_t send = side == 0 ? rg[3] - r0 : r1 - rg[6];
+        const int64_t want = side == 0 ? pi.hi_len : pi.lo_len;
+        if (send != want || send < 0)
+            return fail(DIA_ERR_INVALID, "dia_dist_peer_setup: halo lengths disagree with the "
+                                         "neighbour's window");
+        void* pw = nullptr;
+        DIA_TRY_CUDA(cudaIpcOpenMemHandle(&pw, pi.handle, cudaIpcMemLazyEnablePeerAccess));
+        d->peer_win[side] = pw;
+        const WinLayout pwl = win_layout(pi.lo_len, pi.hi_len);
+        auto* pctl = (unsigned long long*)pw;
+        if (side == 0) {
+            h.has_left = 1;
+            h.peer_left_flag_hi = pctl + 1;
+            for (int p = 0; p < 2; ++p) h.peer_left_halo_hi[p] = (float*)((char*)pw + pwl.hi_off[p]);
+            h.send_left_hi = rg[3] > r0 ? rg[3] : r0;
+        } else {
+            h.has_right = 1;
+            h.peer_right_flag_lo = pctl + 0;
+            for (int p = 0; p < 2; ++p) h.peer_right_halo_lo[p] = (float*)((char*)pw + pwl.lo_off[p]);
+            h.send_right_lo = rg[6] < r1 ? rg[6] : r1;
+        }
+    }
+    d->r0 = r0;
+    d->r1 = r1;
+    d->x_lo = x_lo;
+    d->x_hi = x_hi;
+    d->step = 0;
+    /* no rank may push into a window before its owner has zeroed it */
+    DIA_TRY_CUDA(cudaDeviceSynchronize());
+    int* one = nullptr;
+    DIA_TRY_CUDA(cudaMalloc(&one, sizeof(int)));
+    nr = ncclAllReduce(one, one, 1, ncclInt, ncclSum, d->comm, d->cs);
+    if (nr == ncclSuccess) e = cudaStreamSynchronize(d->cs);
+    cudaFree(one);
+    if (nr != ncclSuccess) return nccl_fail(nr, "dia_dist_peer_setup: barrier");
+    if (e != cudaSuccess) return cuda_fail(e, "dia_dist_peer_setup: barrier");
+    d->peer_ready = true;
+    return DIA_OK;
+}
+
+extern "C" int dia_dist_spmv_fused(DiaDist* d, int64_t n_rows, int64_t n_cols, int K,
+                                   const int* d_offsets, const float* d_vals, int64_t stride,
+                                   int64_t vrow0, int dmin, int dmax, const float* d_x_own,
+                                   float* d_y, cudaStream_t stream)
+{
+    if (!d || !d->peer_ready)
+        return fail(DIA_ERR_INVALID, "dia_dist_spmv_fused: call dia_dist_peer_setup first");
+    const int rc = dia_spmv_rows_peer(&d->ph, d->step + 1, n_rows, n_cols, K, d_offsets, d_vals,
+                                      stride, vrow0, d->r0, d->r1, d->x_lo, d->x_hi, dmin, dmax,
+                                      d_x_own, d_y, stream);
+    if (rc == DIA_OK) ++d->step;
+    return rc;
+}
+
+extern "C" int dia_dist_set_timeout(DiaDist* d, int64_t ns)
+{
+    if (!d || ns <= 0) return fail(DIA_ERR_INVALID, "dia_dist_set_timeout: bad argument");
+    d->ph.timeout_ns = ns;
+    return DIA_OK;
+}
+
+extern "C" int dia_dist_status(DiaDist* d, unsigned int* flags, int clear)
+{
+    if (!d || !flags) return fail(DIA_ERR_INVALID, "dia_dist_status: null pointer");
+    *flags = 0;
+    if (!d->window) return DIA_OK;
+    DIA_TRY_CUDA(cudaMemcpy(flags, d->ph.status, sizeof(unsigned int), cudaMemcpyDeviceToHost));
+    if (clear) DIA_TRY_CUDA(cudaMemset(d->ph.status, 0, sizeof(unsigned int)));
     return DIA_OK;
 }

@@ -174,6 +174,26 @@ class NativeComm:
         from . import check, lib
         check(lib().dia_dist_async_error(self._h))
 
+    def peer_setup(self, halo: "Halo"):
+        """Map the neighbours' receive windows (collective); afterwards
+        dia_dist_spmv_fused moves the x halo inside the step kernel."""
+        from . import check, lib
+        self._ranges = halo.ranges()
+        check(lib().dia_dist_peer_setup(self._h, halo.r0, halo.r1, halo.xlo, halo.xhi,
+                                        self._ranges.ctypes.data))
+
+    def set_timeout(self, seconds: float):
+        from . import check, lib
+        check(lib().dia_dist_set_timeout(self._h, int(seconds * 1e9)))
+
+    def status(self, clear=True) -> int:
+        """DIA_DIST_* bits the step kernels set (DIA_DIST_TIMEOUT = 2)."""
+        import ctypes as C
+        from . import check, lib
+        v = C.c_uint(0)
+        check(lib().dia_dist_status(self._h, C.byref(v), int(clear)))
+        return v.value
+
     def __del__(self):
         from . import _lib
         if getattr(self, "_h", None) and self._h.value and _lib is not None:
@@ -187,18 +207,57 @@ def use_native(group=None):
 
 # ----------------------------------------------------------------- products
 
+DIA_DIST_TIMEOUT = 2
+PEER = 3
+
+
+def _peer_halo_struct():
+    import ctypes as C
+    fp, u64p = C.c_void_p, C.c_void_p
+
+    class PeerHalo(C.Structure):
+        """Mirror of DiaPeerHalo (include/diagpu_b200.h): device pointers of
+        this rank's receive window and of the neighbours' windows."""
+        _fields_ = [("halo_lo", fp * 2), ("halo_hi", fp * 2), ("flag_lo", u64p),
+                    ("flag_hi", u64p), ("push_count", u64p), ("status", fp),
+                    ("peer_left_halo_hi", fp * 2), ("peer_left_flag_hi", u64p),
+                    ("peer_right_halo_lo", fp * 2), ("peer_right_flag_lo", u64p),
+                    ("send_left_hi", C.c_int64), ("send_right_lo", C.c_int64),
+                    ("has_left", C.c_int), ("has_right", C.c_int), ("timeout_ns", C.c_int64)]
+    return PeerHalo
+
+
+PeerHalo = _peer_halo_struct()
+
+
+def spmv_rows_peer(halo: "PeerHalo", step, A: DiaRows, r0, r1, xlo, xhi, x_own, y, stream=None):
+    """One fused peer-halo SpMV step with explicit buffers
+    (dia_spmv_rows_peer); y row i is written at y[i - A.vrow0]."""
+    import ctypes as C
+    from . import _dptr, _stream, check, lib
+    offs = np.asarray(A.offsets)
+    check(lib().dia_spmv_rows_peer(C.byref(halo), step, A.n_rows, A.n_cols, A.K,
+                                   _dptr(A.d_offsets), _dptr(A.vals), A.stride, A.vrow0, r0, r1,
+                                   xlo, xhi, int(offs.min()), int(offs.max()),
+                                   _dptr(x_own, torch.float32), _dptr(y, torch.float32),
+                                   _stream(stream)))
+    return y
+
+
 class DistSpmv:
     """y = A*x with A row-partitioned over the process group.
 
     Each rank holds its row block of A (padded rows layout) and an extended
-    x buffer over its halo window.  With NCCL, `step()` is one library call
-    (dia_dist_spmv_step).  Default overlap=2: halo and boundary strips on the
-    library's high-priority stream, concurrently with the interior rows
-    (fastest measured); 1: boundary strips after the interior on one
-    stream; 0: exchange, then one launch over the block.  Without
-    NCCL (gloo/CPU groups) the exchange goes through torch.distributed."""
+    x buffer over its halo window.  With NCCL, `step()` is one library call.
+    overlap=3 (PEER, the default): one fused kernel per step moves the halo
+    over NVLink itself (dia_dist_spmv_fused; peer windows mapped once at
+    construction).  The NCCL forms (dia_dist_spmv_step): 2, halo and
+    boundary strips on the library's high-priority stream concurrently with
+    the interior rows; 1, boundary strips after the interior on one stream;
+    0, exchange, then one launch over the block.  Without NCCL (gloo/CPU
+    groups) the exchange goes through torch.distributed."""
 
-    def __init__(self, A: DiaRows, halo: Halo, group=None, native=None, overlap=2):
+    def __init__(self, A: DiaRows, halo: Halo, group=None, native=None, overlap=PEER):
         self.A, self.halo, self.group = A, halo, group
         dev = A.vals.device
         self.x_ext = torch.zeros(halo.width, dtype=torch.float32, device=dev)
@@ -208,6 +267,12 @@ class DistSpmv:
         self.native = native
         self.overlap = overlap
         self._ranges = halo.ranges()
+        if self.native is not None and overlap == PEER:
+            if not getattr(self.native, "_peer", False):
+                self.native.peer_setup(halo)
+                self.native._peer = True
+        offs = np.asarray(A.offsets)
+        self._dmin, self._dmax = int(offs.min()), int(offs.max())
 
     @property
     def x_own(self):
@@ -237,6 +302,14 @@ class DistSpmv:
         import ctypes as C
         from . import _dptr, _stream, check, lib
         h, A = self.halo, self.A
+        if self.overlap == PEER:
+            check(lib().dia_dist_spmv_fused(self.native.handle, A.n_rows, A.n_cols, A.K,
+                                            _dptr(A.d_offsets), _dptr(A.vals), A.stride,
+                                            A.vrow0, self._dmin, self._dmax, _dptr(self.x_own),
+                                            _dptr(self.y), _stream()))
+            if launches is not None:
+                launches.append("peer_spmv")
+            return self.y
         a, b = h.interior()
         check(lib().dia_dist_spmv_step(self.native.handle, A.n_rows, A.n_cols, A.K,
                                        _dptr(A.d_offsets), _dptr(A.vals), A.stride, A.vrow0,

@@ -343,6 +343,62 @@ int dia_dist_spmv_step(DiaDist* dist, int64_t n_rows, int64_t n_cols, int num_di
 int dia_dist_async_error(DiaDist* dist);
 int dia_dist_destroy(DiaDist* dist);
 
+/* ---- peer-memory halo: one fused kernel per partitioned SpMV step ----
+ *
+ * No counterpart in the reference (single-GPU only).  The step kernel
+ * itself copies this rank's edge columns of x into its neighbours' receive
+ * buffers over NVLink (peer stores through CUDA IPC mappings), publishes the
+ * step number in the neighbour's flag word, and computes the block's rows:
+ * interior tiles first, boundary tiles last, each boundary tile waiting on
+ * the flag with a time limit.  Receive buffers alternate by step parity.
+ * Bit-identical to the single-GPU SpMV of the whole matrix. */
+enum { DIA_DIST_TIMEOUT = 2 };   /* a flag wait ran out of time */
+
+typedef struct DiaPeerHalo {
+    float* halo_lo[2];              /* this rank's receive buffers, columns [x_lo, r0), by step parity */
+    float* halo_hi[2];              /* columns [r1, x_hi) */
+    unsigned long long* flag_lo;    /* last step whose columns the left neighbour delivered */
+    unsigned long long* flag_hi;    /* ... the right neighbour delivered */
+    unsigned long long* push_count; /* 2 counters (left, right): pushing CTAs finished */
+    unsigned int* status;           /* DIA_DIST_* bits set by the kernel */
+    float* peer_left_halo_hi[2];    /* the left neighbour's halo_hi buffers (peer memory) */
+    unsigned long long* peer_left_flag_hi;
+    float* peer_right_halo_lo[2];   /* the right neighbour's halo_lo buffers */
+    unsigned long long* peer_right_flag_lo;
+    int64_t send_left_hi;           /* columns [r0, send_left_hi) go to the left neighbour */
+    int64_t send_right_lo;          /* columns [send_right_lo, r1) go to the right one */
+    int has_left, has_right;
+    int64_t timeout_ns;             /* limit of one flag wait */
+} DiaPeerHalo;
+
+/* The fused step kernel with every buffer given explicitly (the buffers may
+ * all be local, e.g. to check the kernel on one GPU with the flags already
+ * set).  step counts from 1 and grows by one per call; push_count must have
+ * been zeroed before step 1.  d_x_own holds columns [r0, r1); y row i is
+ * written at d_y[i - vrow0].  dmin/dmax: smallest and largest offset.
+ * At most 128 diagonals; the block needs at least 8 tiles of 1024 rows. */
+int dia_spmv_rows_peer(const DiaPeerHalo* halo, uint64_t step, int64_t n_rows, int64_t n_cols,
+                       int num_diags, const int* d_offsets, const float* d_vals, int64_t stride,
+                       int64_t vrow0, int64_t r0, int64_t r1, int64_t x_lo, int64_t x_hi,
+                       int dmin, int dmax, const float* d_x_own, float* d_y,
+                       cudaStream_t stream);
+/* Collective over the communicator: allocate this rank's receive window
+ * (flags, counters, status, double-buffered halo buffers for [x_lo, r0) and
+ * [r1, x_hi)), exchange CUDA IPC handles with NCCL, map both neighbours'
+ * windows.  h_ranges as for dia_dist_halo_start. */
+int dia_dist_peer_setup(DiaDist* dist, int64_t r0, int64_t r1, int64_t x_lo, int64_t x_hi,
+                        const int64_t* h_ranges);
+/* One partitioned SpMV step through the peer window (after peer_setup). */
+int dia_dist_spmv_fused(DiaDist* dist, int64_t n_rows, int64_t n_cols, int num_diags,
+                        const int* d_offsets, const float* d_vals, int64_t stride,
+                        int64_t vrow0, int dmin, int dmax, const float* d_x_own, float* d_y,
+                        cudaStream_t stream);
+/* Limit of one flag wait (default 2 s). */
+int dia_dist_set_timeout(DiaDist* dist, int64_t ns);
+/* Read (synchronously) the DIA_DIST_* bits of the peer window; clear != 0
+ * resets them. */
+int dia_dist_status(DiaDist* dist, unsigned int* flags, int clear);
+
 /* Device status word shared by the library's kernels.  Kernels that wait on
  * the hardware (the tcgen05 dense-band kernel's mbarrier waits) never spin
  * without bound: on giving up they set a bit here and return early.  Reads

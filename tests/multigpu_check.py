@@ -6,9 +6,11 @@
 Every rank builds its row block of a 27-point-stencil matrix (3D grid
 256 x 256 x 64, offsets up to +-65,793, so every block needs halo rows
 from both neighbours), runs the partitioned SpMV and C = A*A through
-diagpu_b200.dist (NCCL halo exchange, interior rows overlapped with the
-transfer), and compares its rows bit for bit with the same products
-computed for the whole matrix on its own GPU.  Prints one PASS/FAIL line
+diagpu_b200.dist, and compares its rows bit for bit with the same
+products computed for the whole matrix on its own GPU.  SpMV runs four
+steps with a new x each step in every exchange mode: the fused peer-halo
+kernel (halo pushed over NVLink inside the step kernel, receive buffers
+alternating by step parity) and the three NCCL forms.  Prints one PASS/FAIL line
 per rank; exit code 0 only if all ranks pass.
 """
 import os
@@ -35,9 +37,26 @@ def main():
                      for i in (-1, 0, 1)], np.int32)
     h = Halo(n, world, rank, int(offs.min()), int(offs.max()))
     A = dg.DiaRows.synth(n, n, offs, 11, vrow0=h.r0, nrows=h.r1 - h.r0)
-    ds = DistSpmv(A, h)
-    dg.synth_vector(h.r1 - h.r0, 12, i0=h.r0, out=ds.x_own)
-    y = ds.step()[:h.r1 - h.r0].clone()
+    Af = dg.DiaRows.synth(n, n, offs, 11)
+    ok_y = True
+    modes = {3: "peer", 2: "nccl-overlap2", 1: "nccl-overlap1", 0: "nccl-serial"}
+    for mode, name in modes.items():
+        ds = DistSpmv(A, h, overlap=mode)
+        for step in range(4):
+            seed = 12 + 7 * step + 100 * mode
+            dg.synth_vector(h.r1 - h.r0, seed, i0=h.r0, out=ds.x_own)
+            y = ds.step()[:h.r1 - h.r0].clone()
+            yf = dg.spmv(Af, dg.synth_vector(n, seed))[h.r0:h.r1]
+            good = bool(torch.equal(y, yf))
+            if not good:
+                print(f"rank {rank} {name} step {step}: MISMATCH", flush=True)
+            ok_y &= good
+        if mode == 3:
+            st = ds.native.status() if ds.native is not None else 0
+            if st:
+                print(f"rank {rank} peer status {st}", flush=True)
+                ok_y = False
+        del ds
     B_ext = dg.DiaRows.empty(n, n, offs, vrow0=h.xlo, nrows=h.width, zero=True)
     B_ext.vals[:, h.r0 - h.xlo:h.r1 - h.xlo] = A.vals[:, :h.r1 - h.r0]
     dm = DistSpmspm(A, B_ext, h)
@@ -45,11 +64,7 @@ def main():
     torch.cuda.synchronize()
     dist.barrier()
 
-    Af = dg.DiaRows.synth(n, n, offs, 11)
-    xf = dg.synth_vector(n, 12)
-    yf = dg.spmv(Af, xf)[h.r0:h.r1]
     Cf = dg.spmspm(Af, Af)
-    ok_y = bool(torch.equal(y, yf))
     ok_c = np.array_equal(Cf.offsets, dm.C.offsets) and bool(
         torch.equal(Cd, Cf.vals[:, h.r0:h.r1]))
     ok = ok_y and ok_c
