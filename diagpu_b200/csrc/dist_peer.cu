@@ -11,13 +11,13 @@
  *     neighbours' receive buffers (plain stores through CUDA IPC mappings of
  *     the neighbours' memory), then the last of them publishes the step
  *     number in the neighbour's flag word (system-scope release);
- *   - the interior tiles (all columns local) are scheduled first and never
- *     wait;
- *   - the boundary tiles come last in block order; one thread of each spins
- *     on the flag (system-scope acquire) with a time limit, so by the time
- *     they are dispatched the neighbour's columns have normally arrived long
- *     ago and the wait costs nothing.  On time-out the kernel sets
- *     DIA_DIST_TIMEOUT in the status word and finishes without waiting.
+ *   - the interior tiles (all columns local) never wait;
+ *   - the boundary tiles are dispatched a quarter of the way through the
+ *     grid; one thread of each spins on the flag (system-scope acquire) with
+ *     a time limit, so by the time they run the neighbour's columns have
+ *     normally arrived long ago and the wait costs nothing.  On time-out the
+ *     kernel sets DIA_DIST_TIMEOUT in the status word and finishes without
+ *     waiting.
  *
  * Receive buffers are double-buffered by step parity.  Step s writes buffer
  * s & 1; a neighbour can only write that buffer again at step s + 2, which it
@@ -90,7 +90,7 @@ __device__ __forceinline__ void wait_flag(const unsigned long long* flag, unsign
     }
 }
 
-__global__ void __launch_bounds__(kBlock) peer_spmv_kernel(PeerSpmvArgs a)
+__global__ void __launch_bounds__(kBlock, 8) peer_spmv_kernel(PeerSpmvArgs a)
 {
     __shared__ Term s_t[kMaxTerms];
     __shared__ int s_nt;
@@ -131,13 +131,20 @@ __global__ void __launch_bounds__(kBlock) peer_spmv_kernel(PeerSpmvArgs a)
         }
     }
 
-    /* 2. which tile: interior tiles first, boundary tiles last */
+    /* 2. which tile: the boundary tiles are dispatched a quarter of the way
+     * through the grid.  By then the neighbours' pushes (issued at their
+     * kernels' start) have long arrived, and the slower boundary tiles
+     * (split terms) are absorbed by the interior tiles that follow instead
+     * of forming the kernel's tail. */
     const int interior = a.ntiles - a.nlow - a.nhigh;
+    const int nb = a.nlow + a.nhigh;
+    const int first = interior / 4;
     int t;
-    if (b < interior) {
-        t = a.nlow + b;
+    const bool boundary = b >= first && b < first + nb;
+    if (!boundary) {
+        t = a.nlow + (b < first ? b : b - nb);
     } else {
-        const int q = b - interior;
+        const int q = b - first;
         t = q < a.nlow ? q : a.ntiles - a.nhigh + (q - a.nlow);
     }
     const int tile_lo = a.r0 + t * kTile;
@@ -145,44 +152,49 @@ __global__ void __launch_bounds__(kBlock) peer_spmv_kernel(PeerSpmvArgs a)
 
     /* 3. term list: the own-column segment of every diagonal, plus the halo
      * segments that meet this tile (boundary tiles only) */
-    if (threadIdx.x < 32) {
+    if (!boundary) {
+        /* every column of an interior tile is this rank's own */
+        for (int k = threadIdx.x; k < a.K; k += kBlock) {
+            const long long d = a.off[k];
+            const long long own_hi = a.r1 < a.ncols ? a.r1 : a.ncols;
+            long long lo = a.r0 - d, hi = own_hi - d;
+            lo = lo < a.r0 ? a.r0 : lo;
+            hi = hi > a.r1 ? a.r1 : hi;
+            if (hi < lo) hi = lo;
+            Term t;
+            t.u = (long long)k * a.stride - a.vrow0;
+            t.v = d - a.r0;
+            t.lo = (int)lo;
+            t.hi = (int)hi;
+            s_t[k] = t;
+        }
+        if (threadIdx.x == 0) s_nt = a.K;
+    } else if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
         int base = 0;
         for (int k0 = 0; k0 < a.K; k0 += 32) {
             const int k = k0 + lane;
-            Term seg[3];
-            bool ok[3] = {false, false, false};
-            if (k < a.K) {
-                const long long d = a.off[k];
-                const long long u = (long long)k * a.stride - a.vrow0;
-                /* column ranges of the three sources and their V offsets
-                 * relative to x_own (element units; the halo buffers are
-                 * other allocations, reached through the flat address
-                 * space) */
+            /* rows whose column i + d lies in source s (0: left halo,
+             * 1: own block, 2: right halo), clipped to the block's rows */
+            const long long d = k < a.K ? a.off[k] : 0;
+            auto rows_of = [&](int s, long long& lo, long long& hi) {
                 const long long own_hi = a.r1 < a.ncols ? a.r1 : a.ncols;
                 const long long xhi = a.xhi < a.ncols ? a.xhi : a.ncols;
-                const long long clo[3] = {a.xlo, a.r0, a.r1};
-                const long long chi[3] = {a.r0, own_hi, xhi};
-                const float* hl = a.h.halo_lo[par];
-                const float* hh = a.h.halo_hi[par];
-                const long long vb[3] = {hl ? (long long)(hl - a.x_own) - a.xlo : 0,
-                                         -(long long)a.r0,
-                                         hh ? (long long)(hh - a.x_own) - a.r1 : 0};
+                const long long c0 = s == 0 ? a.xlo : (s == 1 ? a.r0 : a.r1);
+                const long long c1 = s == 0 ? a.r0 : (s == 1 ? own_hi : xhi);
+                lo = c0 - d;
+                hi = c1 - d;
+                lo = lo < a.r0 ? a.r0 : lo;
+                hi = hi > a.r1 ? a.r1 : hi;
+                return k < a.K && hi > lo && lo < tile_hi && hi > tile_lo;
+            };
+            unsigned okm = 0;
 #pragma unroll
-                for (int s = 0; s < 3; ++s) {
-                    /* rows whose column i + d lies in the source, clipped
-                     * to the block's rows */
-                    long long lo = clo[s] - d, hi = chi[s] - d;
-                    lo = lo < a.r0 ? a.r0 : lo;
-                    hi = hi > a.r1 ? a.r1 : hi;
-                    ok[s] = hi > lo && lo < tile_hi && hi > tile_lo;
-                    seg[s].u = u;
-                    seg[s].v = vb[s] + d;
-                    seg[s].lo = (int)lo;
-                    seg[s].hi = (int)hi;
-                }
+            for (int s = 0; s < 3; ++s) {
+                long long lo, hi;
+                okm |= rows_of(s, lo, hi) ? 1u << s : 0u;
             }
-            const int cnt = (int)ok[0] + (int)ok[1] + (int)ok[2];
+            const int cnt = __popc(okm);
             /* exclusive prefix of the per-lane counts keeps diagonal order */
             int pre = cnt;
 #pragma unroll
@@ -193,8 +205,27 @@ __global__ void __launch_bounds__(kBlock) peer_spmv_kernel(PeerSpmvArgs a)
             const int tot = __shfl_sync(0xffffffffu, pre, 31);
             int pos = base + pre - cnt;
 #pragma unroll
-            for (int s = 0; s < 3; ++s)
-                if (ok[s]) s_t[pos++] = seg[s];
+            for (int s = 0; s < 3; ++s) {
+                if (!(okm >> s & 1u)) continue;
+                long long lo, hi;
+                rows_of(s, lo, hi);
+                /* V offsets relative to x_own, in elements; the halo
+                 * buffers are other allocations, reached through the flat
+                 * address space */
+                long long vb;
+                if (s == 1)
+                    vb = -(long long)a.r0;
+                else if (s == 0)
+                    vb = (long long)(a.h.halo_lo[par] - a.x_own) - a.xlo;
+                else
+                    vb = (long long)(a.h.halo_hi[par] - a.x_own) - a.r1;
+                Term t;
+                t.u = (long long)k * a.stride - a.vrow0;
+                t.v = vb + d;
+                t.lo = (int)lo;
+                t.hi = (int)hi;
+                s_t[pos++] = t;
+            }
             base += tot;
         }
         if (lane == 0) s_nt = base;

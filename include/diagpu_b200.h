@@ -348,9 +348,9 @@ int dia_dist_destroy(DiaDist* dist);
  * No counterpart in the reference (single-GPU only).  The step kernel
  * itself copies this rank's edge columns of x into its neighbours' receive
  * buffers over NVLink (peer stores through CUDA IPC mappings), publishes the
- * step number in the neighbour's flag word, and computes the block's rows:
- * interior tiles first, boundary tiles last, each boundary tile waiting on
- * the flag with a time limit.  Receive buffers alternate by step parity.
+ * step number in the neighbour's flag word, and computes the block's rows;
+ * the boundary tiles, dispatched a quarter of the way through the grid,
+ * wait on the flag with a time limit.  Receive buffers alternate by step parity.
  * Bit-identical to the single-GPU SpMV of the whole matrix. */
 enum { DIA_DIST_TIMEOUT = 2 };   /* a flag wait ran out of time */
 
