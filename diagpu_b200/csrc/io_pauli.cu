@@ -29,29 +29,59 @@
 
 namespace {
 
-/* every offset sum_k s_k 2^k over the bits k of x, s_k = +1 or -1 */
+constexpr size_t kMaxDiags = (size_t)1 << 16;
+/* pattern-to-diagonal tables of all distinct X masks together */
+constexpr size_t kMaxPatterns = (size_t)1 << 26;
+
+/* every offset sum_k s_k 2^k over the bits k of x, s_k = +1 or -1, in
+ * ascending order (x has at most 16 bits here, so at most 65536 offsets) */
 void string_offsets(uint64_t x, std::vector<int64_t>& out)
 {
-    std::vector<int64_t> acc{0};
+    out.assign(1, 0);
     for (int k = 0; k < 64; ++k) {
         if (!((x >> k) & 1)) continue;
         const int64_t w = (int64_t)1 << k;
-        std::vector<int64_t> next;
-        next.reserve(acc.size() * 2);
-        for (int64_t a : acc) {
-            next.push_back(a + w);
-            next.push_back(a - w);
+        const size_t m = out.size();
+        out.resize(2 * m);
+        for (size_t i = 0; i < m; ++i) {
+            out[m + i] = out[i] + w;
+            out[i] -= w;
         }
-        acc.swap(next);
     }
-    out.insert(out.end(), acc.begin(), acc.end());
+    std::sort(out.begin(), out.end());
 }
+
+int pauli_to_dia(int nq, int nterms, const uint64_t* h_x_mask, const uint64_t* h_z_mask,
+                 const double* h_coef_re, const double* h_coef_im, int* num_diags,
+                 int* h_offsets, float* h_vals, int64_t stride, int* is_real);
 
 }  // namespace
 
 using namespace dia;
 
+/* Host memory use is bounded before anything large is built: a string with
+ * more than 16 X/Y factors alone spans more than 65536 diagonals and is
+ * rejected at once, the offset set is merged term by term and the call
+ * stops as soon as it passes 65536, and the per-mask pattern tables are
+ * shared by terms with the same X mask and capped in total.  An allocation
+ * failure anyway becomes DIA_ERR_UNSUPPORTED instead of an exception
+ * leaving the C interface. */
 extern "C" int dia_pauli_to_dia(int nq, int nterms, const uint64_t* h_x_mask,
+                                const uint64_t* h_z_mask, const double* h_coef_re,
+                                const double* h_coef_im, int* num_diags, int* h_offsets,
+                                float* h_vals, int64_t stride, int* is_real)
+{
+    try {
+        return pauli_to_dia(nq, nterms, h_x_mask, h_z_mask, h_coef_re, h_coef_im, num_diags,
+                            h_offsets, h_vals, stride, is_real);
+    } catch (const std::bad_alloc&) {
+        return fail(DIA_ERR_UNSUPPORTED, "dia_pauli_to_dia: out of host memory");
+    }
+}
+
+namespace {
+
+int pauli_to_dia(int nq, int nterms, const uint64_t* h_x_mask,
                                 const uint64_t* h_z_mask, const double* h_coef_re,
                                 const double* h_coef_im, int* num_diags, int* h_offsets,
                                 float* h_vals, int64_t stride, int* is_real)
@@ -65,13 +95,32 @@ extern "C" int dia_pauli_to_dia(int nq, int nterms, const uint64_t* h_x_mask,
     for (int t = 0; t < nterms; ++t)
         if ((h_x_mask[t] | h_z_mask[t]) & ~all)
             return fail(DIA_ERR_INVALID, "dia_pauli_to_dia: a string acts on a qubit >= nq");
-    std::vector<int64_t> offs;
-    for (int t = 0; t < nterms; ++t) string_offsets(h_x_mask[t], offs);
-    std::sort(offs.begin(), offs.end());
-    offs.erase(std::unique(offs.begin(), offs.end()), offs.end());
-    if (offs.size() > ((size_t)1 << 16))
-        return fail(DIA_ERR_UNSUPPORTED, "dia_pauli_to_dia: more than 65536 diagonals (strings "
-                                         "with many X/Y are not banded; DIA does not suit them)");
+    static const char* kTooMany =
+        "dia_pauli_to_dia: more than 65536 diagonals (strings with many X/Y are not banded; "
+        "DIA does not suit them)";
+    for (int t = 0; t < nterms; ++t)
+        if (__builtin_popcountll(h_x_mask[t]) > 16) return fail(DIA_ERR_UNSUPPORTED, kTooMany);
+    /* distinct X masks: terms sharing one share its offsets and tables */
+    std::vector<uint64_t> masks(h_x_mask, h_x_mask + nterms);
+    std::sort(masks.begin(), masks.end());
+    masks.erase(std::unique(masks.begin(), masks.end()), masks.end());
+    size_t patterns = 0;
+    for (uint64_t x : masks) {
+        patterns += (size_t)1 << __builtin_popcountll(x);
+        if (patterns > kMaxPatterns)
+            return fail(DIA_ERR_UNSUPPORTED, "dia_pauli_to_dia: too many distinct X/Y patterns "
+                                             "(more than 2^26 pattern-table entries)");
+    }
+    std::vector<int64_t> offs, one, merged;
+    for (uint64_t x : masks) {
+        string_offsets(x, one);
+        merged.resize(offs.size() + one.size());
+        merged.erase(std::set_union(offs.begin(), offs.end(), one.begin(), one.end(),
+                                    merged.begin()),
+                     merged.end());
+        offs.swap(merged);
+        if (offs.size() > kMaxDiags) return fail(DIA_ERR_UNSUPPORTED, kTooMany);
+    }
     const int K = (int)offs.size();
     if (!h_offsets && !h_vals) {
         *num_diags = K;
@@ -100,10 +149,14 @@ extern "C" int dia_pauli_to_dia(int nq, int nterms, const uint64_t* h_x_mask,
      * Those bits, compressed to a pattern p (bit j of p = j-th set bit of
      * x), come from four byte tables; kof[p] is the pattern's diagonal
      * index.  No hashing per row. */
-    std::vector<uint32_t> byte_tab((size_t)nterms * 4 * 256);
-    std::vector<std::vector<int>> kof((size_t)nterms);
-    for (int t = 0; t < nterms; ++t) {
-        const uint64_t x = h_x_mask[t];
+    std::vector<uint32_t> byte_tab(masks.size() * 4 * 256);
+    std::vector<std::vector<int>> kof(masks.size());
+    std::vector<int> mask_of((size_t)nterms);
+    for (int t = 0; t < nterms; ++t)
+        mask_of[(size_t)t] = (int)(std::lower_bound(masks.begin(), masks.end(), h_x_mask[t]) -
+                                   masks.begin());
+    for (size_t t = 0; t < masks.size(); ++t) {
+        const uint64_t x = masks[t];
         int bits[64], nb = 0;
         for (int k = 0; k < 64; ++k)
             if ((x >> k) & 1) bits[nb++] = k;
@@ -135,8 +188,9 @@ extern "C" int dia_pauli_to_dia(int nq, int nterms, const uint64_t* h_x_mask,
         std::fill(acc.begin(), acc.end(), std::complex<double>(0.0, 0.0));
         for (int t = 0; t < nterms; ++t) {
             const uint64_t x = h_x_mask[t], z = h_z_mask[t];
-            const uint32_t* tab = &byte_tab[(size_t)t * 4 * 256];
-            const int* kt = kof[t].data();
+            const int m = mask_of[(size_t)t];
+            const uint32_t* tab = &byte_tab[(size_t)m * 4 * 256];
+            const int* kt = kof[(size_t)m].data();
             const std::complex<double> c = coef[t], mc = -coef[t];
             for (int64_t r = r0; r < r0 + chunk; ++r) {
                 const uint64_t col = (uint64_t)r ^ x;
@@ -160,3 +214,5 @@ extern "C" int dia_pauli_to_dia(int nq, int nterms, const uint64_t* h_x_mask,
     if (is_real) *is_real = real ? 1 : 0;
     return DIA_OK;
 }
+
+}  // namespace

@@ -96,3 +96,35 @@ def test_errors():
     with pytest.raises(dg.DiaError) as e:             # 2^17 diagonals: not banded
         dg.pauli_to_dia_host([(1.0, " ".join(f"X{k}" for k in range(17)))], 17)
     assert e.value.code == dg.DIA_ERR_UNSUPPORTED
+
+
+def test_wide_strings_rejected_without_enumerating():
+    """A 30-qubit all-X string spans 2^30 diagonals: rejected at once with
+    DIA_ERR_UNSUPPORTED (no multi-GiB offset list is built first)."""
+    import time
+    t0 = time.perf_counter()
+    with pytest.raises(dg.DiaError) as e:
+        dg.pauli_to_dia_host([(1.0, " ".join(f"X{q}" for q in range(30)))], 30)
+    assert e.value.code == dg.DIA_ERR_UNSUPPORTED
+    assert time.perf_counter() - t0 < 5.0
+
+
+def test_many_sixteen_x_strings_stop_at_the_cap():
+    """Each string has 16 X factors (65536 diagonals, allowed alone); their
+    union passes 65536 and the call stops with DIA_ERR_UNSUPPORTED."""
+    terms = [(1.0, " ".join(f"X{q}" for q in range(s, s + 16))) for s in range(8)]
+    with pytest.raises(dg.DiaError) as e:
+        dg.pauli_to_dia_host(terms, 24)
+    assert e.value.code == dg.DIA_ERR_UNSUPPORTED
+
+
+def test_terms_sharing_an_x_mask_share_tables():
+    """Many terms on one X mask with different Z masks: still exact."""
+    rng = np.random.default_rng(7)
+    terms = []
+    for _ in range(30):
+        zs = [f"Z{q}" for q in (2, 3, 4) if rng.random() < 0.5]
+        terms.append((rng.standard_normal(), " ".join(["X0", "Y1"] + zs)))
+    n, offs, vals, real = dg.pauli_to_dia_host(terms, 5)
+    ref = dense(terms, 5).astype(np.complex64)
+    assert np.allclose(from_dia(n, offs, vals), ref, atol=1e-5)
