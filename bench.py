@@ -39,6 +39,7 @@ sys.path.insert(0, ROOT)
 N5 = 256 * 256 * 1024
 OFF5 = np.array([i + 256 * j + 65536 * k for k in (-1, 0, 1) for j in (-1, 0, 1)
                  for i in (-1, 0, 1)], np.int32)
+OFF2 = np.array([-16384, -128, -1, 0, 1, 128, 16384], np.int32)
 SEED_A, SEED_X = 5001, 5002
 REF_SAMPLE_ROWS = 4 * 1024 * 1024
 # DRAM bytes (read + write) of one spmv_kernel launch on config 5, derived
@@ -215,12 +216,40 @@ def roofline(achieved_gbs, hbm, src, traffic=None):
             "frac": round(achieved_gbs / hbm, 4), "peak_source": src, "traffic": traffic}
 
 
+def hm_of(A):
+    """The HM arrays (values, int64 starts, offsets, lengths) of a whole
+    rows-layout matrix, on the device."""
+    n = A.n_rows
+    ln = (n - np.abs(A.offsets.astype(np.int64))).astype(np.int64)
+    st = np.concatenate([[0], np.cumsum(ln[:-1])]).astype(np.int64)
+    val = torch.empty(int(ln.sum()), device="cuda")
+    for k, d in enumerate(A.offsets):
+        r0 = -min(int(d), 0)
+        val[int(st[k]):int(st[k] + ln[k])] = A.vals[k, r0:r0 + int(ln[k])]
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    return val, t(st), t(A.offsets.astype(np.int32)), t(ln.astype(np.int32))
+
+
 def secondary_spmspm(dg, name, n, A, B, steps, warmup, hbm, src, flush=None):
     sym = dg.spmspm_symbolic(n, A.offsets, B.offsets)
     plan = dg.SpmspmPlan(A, B)
     Cm = plan.new_C()
     fn = lambda: plan.execute(A, B, Cm)
     ms = timed(fn, steps, warmup, flush=flush, per_launch=flush is not None)
+    # the same product through the reference's HM argument set (the
+    # counterpart of gather_meta_kernel's launch)
+    av, ast, aoff, aln = hm_of(A)
+    bv, bst, boff, bln = (av, ast, aoff, aln) if B is A else hm_of(B)
+    lk = np.full(2 * n - 1, -1, np.int32)
+    lk[B.offsets.astype(np.int64) + n - 1] = np.arange(B.K, dtype=np.int32)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    dlk, dcs = t(lk), t(sym["C_start"].astype(np.int64))
+    dco, dcl = t(sym["C_off"].astype(np.int32)), t(sym["C_len"].astype(np.int32))
+    Chm = torch.empty(int(sym["C_len"].astype(np.int64).sum()), device="cuda")
+    hm_ms = timed(lambda: dg.spmspm_hm(av, ast, aoff, aln, bv, bst, bln, dlk, Chm, dcs, dco, dcl,
+                                       n), steps, warmup, flush=flush,
+                  per_launch=flush is not None)
+    del av, bv, Chm
     nnzA = nnz_rows(n, A.offsets, 0, n)
     nnzB = 0 if B is A else nnz_rows(n, B.offsets, 0, n)
     nnzC = int(sym["C_len"].astype(np.int64).sum())
@@ -230,6 +259,7 @@ def secondary_spmspm(dg, name, n, A, B, steps, warmup, hbm, src, flush=None):
     return {"workload": name, "metric": "spmspm_useful_GFLOPs", "value": round(fl / ms / 1e6, 2),
             "unit": "GFLOP/s", "ms": round(ms, 4), "bytes": byts, "useful_flops": fl,
             "c_diagonals": len(sym["C_off"]), "pairs": len(sym["pair_a"]),
+            "hm_args_ms": round(hm_ms, 4),
             "roofline": roofline(byts / ms / 1e6, hbm, src), "gpu_launches_per_step": 2}
 
 
@@ -622,6 +652,144 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+# ------------------------------------------------- reference GPU kernels
+
+def _hm_structure(n, offs):
+    """HM layout of a diagonal set: lengths n - |d| and prefix-sum starts."""
+    offs = np.asarray(offs, np.int64)
+    ln = (n - np.abs(offs)).astype(np.int64)
+    st = np.concatenate([[0], np.cumsum(ln[:-1])]).astype(np.int64)
+    return ln, st
+
+
+def _sumset(n, a, b):
+    """Ascending {da + db : |da + db| < n} (the output diagonals)."""
+    s = np.unique((np.asarray(a, np.int64)[:, None] + np.asarray(b, np.int64)[None, :]).ravel())
+    return s[np.abs(s) < n]
+
+
+def reference_gpu_leg(steps, warmup):
+    """The reference's own GPU kernels, compiled from its sources into
+    oracle/_ref, timed on this GPU on the workloads the library's own arm
+    times (same shapes; values from torch's seeded generator):
+      tc_spmv_regdirect (spmv/src/tc_spmv_regdirect_kernel.cu:62-147) on
+        config 5 in its Recon layout;
+      gather_meta_kernel<512> (spmspm/spmspm.cu:256-319) and the Haque HM
+        atomic kernel (spmspm/paper_hm_kernel.cu:31-93; C zeroed per launch
+        as its bench does) on configs 2 and 3;
+      gemm_diag_kernel (gemm_diag/gemm_diag.cu:119-329) on config 4, timed
+        with its memset as gemm_diag.cu:553-566 times it.
+    Each entry is one JSON line; times are mean ms per launch (CUDA events,
+    back to back after warm-up)."""
+    import ctypes as C
+
+    import oracle
+    torch.cuda.set_device(0)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(7)
+    P = lambda t: C.c_void_p(t.data_ptr())
+    S = lambda: C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    uni = lambda shape: torch.rand(shape, generator=gen, device="cuda") * 2 - 1
+    reps = max(3, min(steps, 20))
+    out = []
+
+    def tm(fn, it=reps):
+        return timed(fn, it, max(1, min(warmup, 3)))
+
+    R = oracle.ref("spmv")
+    if R is not None:
+        R.ref_launch_tc_spmv.argtypes = [C.c_int] * 3 + [C.c_void_p] * 3 + [C.c_int,
+                                                                           C.c_void_p,
+                                                                           C.c_void_p]
+        n = N5
+        desc = np.sort(OFF5)[::-1].astype(np.int32)
+        rec = uni((len(desc), n))
+        x, y = uni((n,)), torch.empty(n, device="cuda")
+        doff = t(desc)
+        ms = tm(lambda: R.ref_launch_tc_spmv(n, n, len(desc), P(doff), P(rec), P(x), n, P(y),
+                                             S()))
+        b, _ = spmv_bytes(n, OFF5, 0, n)
+        out.append({"kernel": "tc_spmv_regdirect (TF32 mma.sync)",
+                    "workload": "config5 SpMV, Recon layout", "ms": round(ms, 4),
+                    "GBps": round(b / ms / 1e6, 1)})
+        del rec, x, y
+        torch.cuda.empty_cache()
+    M = oracle.ref("spmspm")
+    if M is not None:
+        M.ref_launch_gather_meta.argtypes = ([C.c_void_p] * 4 + [C.c_int] + [C.c_void_p] * 8 +
+                                             [C.c_int, C.c_int, C.c_void_p])
+        M.ref_launch_hm.argtypes = ([C.c_void_p] * 4 + [C.c_int] + [C.c_void_p] * 4 + [C.c_int] +
+                                    [C.c_void_p] * 4 + [C.c_int, C.c_void_p, C.c_int, C.c_int,
+                                                        C.c_void_p])
+        for name, n, oa, ob in (("config2 3D 7-pt 128^3 C=A*A", 128 ** 3, OFF2, OFF2),
+                                ("config3 scattered 32x32 offsets n=1e6 C=A*B", 1_000_000,
+                                 _scat(301), _scat(302))):
+            al, ast = _hm_structure(n, oa)
+            bl, bst = _hm_structure(n, ob)
+            co = _sumset(n, oa, ob)
+            cl, cs = _hm_structure(n, co)
+            av = uni((int(al.sum()),))
+            bv = av if ob is oa else uni((int(bl.sum()),))
+            nnzC = int(cl.sum())
+            lk = np.full(2 * n - 1, -1, np.int32)
+            lk[np.asarray(ob) + n - 1] = np.arange(len(ob), dtype=np.int32)
+            clk = np.full(2 * n - 1, -1, np.int32)
+            clk[co + n - 1] = np.arange(len(co), dtype=np.int32)
+            i32 = lambda a: t(np.asarray(a).astype(np.int32))
+            dao, dbo, dco = i32(oa), i32(ob), i32(co)
+            dal, dbl, dcl = i32(al), i32(bl), i32(cl)
+            das, dbs, dcs = (t(np.asarray(v, np.uint64)) for v in (ast, bst, cs))
+            das32, dbs32, dcs32 = i32(ast), i32(bst), i32(cs)
+            dlk, dclk = t(lk), t(clk)
+            Cv = torch.zeros(nnzC, device="cuda")
+            gm = tm(lambda: M.ref_launch_gather_meta(P(av), P(das), P(dao), P(dal), len(oa),
+                                                     P(bv), P(dbs), P(dbl), P(dlk), P(Cv),
+                                                     P(dcs), P(dco), P(dcl), len(co), n, S()))
+            nzA = int(al.sum())
+
+            def hm():
+                Cv.zero_()
+                M.ref_launch_hm(P(av), P(dao), P(das32), P(dal), len(oa), P(bv), P(dbo),
+                                P(dbs32), P(dbl), len(ob), P(Cv), P(dco), P(dcs32), P(dcl),
+                                len(co), P(dclk), nzA, n, S())
+            hm_ms = tm(hm)
+            byts = 4 * (int(al.sum()) + (0 if ob is oa else int(bl.sum())) + nnzC)
+            out.append({"kernel": "gather_meta_kernel<512>", "workload": name,
+                        "ms": round(gm, 4), "GBps": round(byts / gm / 1e6, 1)})
+            out.append({"kernel": "hm_structured_sparse_matmul_kernel (atomics, C zeroed)",
+                        "workload": name, "ms": round(hm_ms, 4),
+                        "GBps": round(byts / hm_ms / 1e6, 1)})
+            del av, bv, Cv
+            torch.cuda.empty_cache()
+    G = oracle.ref("gemm_diag")
+    if G is not None:
+        G.ref_launch_gemm_diag.argtypes = ([C.c_void_p] * 4 + [C.c_int] * 3 + [C.c_void_p] * 4 +
+                                           [C.c_void_p])
+        n, hb = 262144, 64
+        goff = np.arange(-hb, hb + 1, dtype=np.int32)
+        DA, DB = uni((len(goff), n)), uni((len(goff), n))
+        ks = _sumset(n, goff, goff)
+        cl, cs = _hm_structure(n, ks)
+        k2i = np.full(2 * n - 1, -1, np.int32)
+        k2i[ks + n - 1] = np.arange(len(ks), dtype=np.int32)
+        dco, dcl, dk2i, doff = t(cs.astype(np.int32)), t(cl.astype(np.int32)), t(k2i), t(goff)
+        Cg = torch.zeros(int(cl.sum()), device="cuda")
+
+        def gd():
+            Cg.zero_()
+            G.ref_launch_gemm_diag(P(DA), P(DB), P(doff), P(doff), len(goff), len(goff), n,
+                                   P(Cg), P(dco), P(dcl), P(dk2i), S())
+        ms = tm(gd, max(3, reps // 2))
+        byts = 4 * (2 * nnz_rows(n, goff, 0, n) + int(cl.sum()))
+        out.append({"kernel": "gemm_diag_kernel (with its memset)",
+                    "workload": "config4 dense band hb=64 n=262144 gemm_diag",
+                    "ms": round(ms, 4), "GBps": round(byts / ms / 1e6, 1)})
+        del DA, DB, Cg
+        torch.cuda.empty_cache()
+    return out
+
+
 def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -662,6 +830,9 @@ def run_reference(args):
     ms = call(args.steps)
     b, _ = spmv_bytes(N5, OFF5, 0, S)
     v = round(b / ms / 1e6, 2)
+    if world == 1 and torch.cuda.is_available() and not args.no_ref_gpu:
+        for entry in reference_gpu_leg(args.steps, args.warmup):
+            emit({"reference_gpu": entry})
     print(json.dumps({
         "impl": "reference", "metric": "spmv_GBps", "value": v, "unit": "GB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
@@ -837,6 +1008,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ref-gpu", action="store_true",
+                    help="reference arm: skip the reference's GPU kernels")
     ap.add_argument("--only", choices=sorted(ONLY), default=None,
                     help="run one workload `steps` times (for profiling) and print its time")
     args = ap.parse_args()

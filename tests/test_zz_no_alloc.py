@@ -72,3 +72,49 @@ def test_noalloc_rejects_plans_beyond_the_static_buffer():
     rc = L.dia_spmspm_hm_noalloc(*a)
     assert rc == dg.DIA_ERR_CAPACITY
     assert "static buffer" in L.dia_last_error().decode()
+
+
+def _device_memory_state():
+    """(free bytes, mempool reserved bytes, mempool used bytes) of the current
+    device, read through the driver API: cuMemGetInfo and the attributes of
+    the device's current memory pool, the pool cudaMallocAsync draws from."""
+    cu = C.CDLL("libcuda.so.1")
+    free, total = C.c_size_t(0), C.c_size_t(0)
+    assert cu.cuMemGetInfo_v2(C.byref(free), C.byref(total)) == 0
+    dev, pool = C.c_int(0), C.c_void_p()
+    assert cu.cuCtxGetDevice(C.byref(dev)) == 0
+    assert cu.cuDeviceGetMemPool(C.byref(pool), dev) == 0
+    reserved, used = C.c_uint64(0), C.c_uint64(0)
+    assert cu.cuMemPoolGetAttribute(pool, 5, C.byref(reserved)) == 0   # RESERVED_MEM_CURRENT
+    assert cu.cuMemPoolGetAttribute(pool, 7, C.byref(used)) == 0       # USED_MEM_CURRENT
+    return free.value, reserved.value, used.value
+
+
+def test_noalloc_leaves_device_memory_untouched(golden):
+    """The property the entry point exists for: a call changes neither the
+    device's free memory nor the stream-ordered pool, while the allocating
+    entry point draws its scratch from that pool."""
+    L = dg.lib()
+    g, name = golden["spmspm_scatter"], "n600_k32"
+    A, B = _hm(g, name, "A"), _hm(g, name, "B")
+    n = int(A[1][A[0] == 0][0])
+    Cs = (g[f"{name}__C_off"], g[f"{name}__C_len"], g[f"{name}__C_start"])
+    nnz = int(Cs[2][-1] + Cs[1][-1])
+    Cv = torch.zeros(nnz, device="cuda")
+    a, keep = _args(n, A, B, Cs, Cv)
+    dg.check(L.dia_spmspm_hm_noalloc(*a))     # first call on the device: address lookup
+    torch.cuda.synchronize()
+    before = _device_memory_state()
+    for _ in range(3):
+        dg.check(L.dia_spmspm_hm_noalloc(*a))
+    torch.cuda.synchronize()
+    assert _device_memory_state() == before
+    dg.check(L.dia_spmspm_hm(*a))
+    torch.cuda.synchronize()
+    used_high = C.c_uint64(0)
+    cu = C.CDLL("libcuda.so.1")
+    dev, pool = C.c_int(0), C.c_void_p()
+    cu.cuCtxGetDevice(C.byref(dev))
+    cu.cuDeviceGetMemPool(C.byref(pool), dev)
+    assert cu.cuMemPoolGetAttribute(pool, 8, C.byref(used_high)) == 0   # USED_MEM_HIGH
+    assert used_high.value > 0, "the allocating entry point should draw from the pool"
