@@ -15,9 +15,10 @@
  * transfer and then the two boundary strips run there, concurrently with
  * the interior rows' kernel (local columns only) on the caller's stream,
  * and their CTAs are dispatched ahead of the interior kernel's pending
- * ones.  Measured on 8 B200s (config 5): 0.166 ms per step against 0.185
- * ms for exchange-then-one-launch and 0.211 ms for boundary strips after
- * the interior on one stream.
+ * ones.  The driver's 8-GPU run of this form (config 5) measured 0.218
+ * ms per step against 0.172 ms for the block's kernel alone; the exchange
+ * and the strips, not the kernel, were the cost, which is why the default
+ * step is now the fused peer-halo kernel of dist_peer.cu.
  * The reference has no multi-GPU path (its programs run on one device).
  */
 #include <nccl.h>
