@@ -28,6 +28,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libdiagpu_b200.so")
 
 DIA_OK, DIA_ERR_INVALID, DIA_ERR_CUDA, DIA_ERR_UNSUPPORTED, DIA_ERR_CAPACITY = range(5)
+DIA_TC_TIMEOUT = 1   # dia_device_status bit: a tcgen05 kernel wait ran out
 GEMM_AUTO, GEMM_SIMT, GEMM_TCGEN05 = 0, 1, 2
 ALIGN = 32  # floats per stride unit (128 bytes)
 
@@ -89,6 +90,8 @@ def lib():
             getattr(L, name).restype = i
         L.dia_device_status.argtypes = [p, i]
         L.dia_device_status.restype = i
+        L.dia_test_tc_wait.argtypes = [u64, i]
+        L.dia_test_tc_wait.restype = i
         L.dia_synth_rows.argtypes = [u64, i64, i64, i, p, p, i, f, f, i64, i64, i64, p, p]
         L.dia_synth_vector.argtypes = [u64, i64, i64, f, f, p, p]
         L.dia_lanczos_workspace.argtypes = [i64]

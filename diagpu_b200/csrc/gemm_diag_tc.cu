@@ -441,6 +441,13 @@ constexpr int kMaxWin = kECols / kWinCols;
 constexpr int kEbPitch = kWinCols + 1;
 constexpr int kEbFloats = kTcRows * kEbPitch + 32;
 constexpr unsigned long long kWsWaitNs = 2000000000ull;
+/* Limit of every wait of the warp-specialised kernel (kWsWaitNs unless a
+ * test lowers it), and a test switch: when set, one skew warp of CTA 0
+ * withholds its first operand-ready arrival, so the MMA issuer's wait runs
+ * out and the kernel must take its abort path (stop every role, let issued
+ * copies land, free tensor memory) and report DIA_TC_TIMEOUT. */
+static __device__ unsigned long long g_ws_wait_ns = kWsWaitNs;
+static __device__ int g_ws_withhold;
 
 struct WsArgs {
     float* C;
@@ -496,7 +503,7 @@ __device__ bool ws_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag)
             const unsigned long long t = global_ns();
             if (t0 == 0)
                 t0 = t;
-            else if (t - t0 > kWsWaitNs) {
+            else if (t - t0 > g_ws_wait_ns) {
                 *abort_flag = 1;
                 atomicOr(&g_device_status, (unsigned)DIA_TC_TIMEOUT);
                 return false;
@@ -511,7 +518,7 @@ __device__ void ws_drain(uint32_t bar, uint32_t parity)
 {
     const unsigned long long t0 = global_ns();
     while (!mbar_try(bar, parity))
-        if (global_ns() - t0 > kWsWaitNs) {
+        if (global_ns() - t0 > g_ws_wait_ns) {
             atomicOr(&g_device_status, (unsigned)DIA_TC_TIMEOUT);
             return;
         }
@@ -838,7 +845,8 @@ gemm_diag_ws_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
                 if (lane == 0) {
-                    mbar_arrive(bar(bars.op_full[s]));
+                    if (!(g_ws_withhold && blockIdx.x == 0 && sw == 0 && go == 0))
+                        mbar_arrive(bar(bars.op_full[s]));
                     mbar_arrive(bar(bars.empty_b[sb]));
                     for (int q = ws_qlo(j, a.P, a.nchunks); q < ws_qlo(j + 1, a.P, a.nchunks); ++q)
                         mbar_arrive(bar(bars.empty_a[(ga0 + q) % kARing]));
@@ -1091,5 +1099,15 @@ extern "C" int dia_device_status(unsigned int* flags, int clear)
         const unsigned int z = 0;
         DIA_TRY_CUDA(cudaMemcpyToSymbol(dia::g_device_status, &z, sizeof(unsigned int)));
     }
+    return DIA_OK;
+}
+
+extern "C" int dia_test_tc_wait(uint64_t wait_ns, int withhold)
+{
+    if (wait_ns == 0) wait_ns = dia::kWsWaitNs;
+    const unsigned long long ns = wait_ns;
+    const int w = withhold ? 1 : 0;
+    DIA_TRY_CUDA(cudaMemcpyToSymbol(dia::g_ws_wait_ns, &ns, sizeof(ns)));
+    DIA_TRY_CUDA(cudaMemcpyToSymbol(dia::g_ws_withhold, &w, sizeof(w)));
     return DIA_OK;
 }

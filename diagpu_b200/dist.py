@@ -370,3 +370,62 @@ class DistSpmspm:
 def offsets_span(offsets):
     o = np.asarray(offsets)
     return int(o.min()), int(o.max())
+
+
+class PeerLost(RuntimeError):
+    """A neighbour stopped taking part (left, or missed its heartbeat)."""
+
+
+class Heartbeat:
+    """Host-side liveness of the ranks of a partitioned product.
+
+    Before each step a rank publishes the step it is about to run in the
+    process group's key-value store and waits, at most `timeout` seconds,
+    until both neighbours have published the same step (every rank
+    publishes before it waits, so the handshake cannot deadlock).  A rank
+    that leaves between steps (calls leave(), or simply stops) is therefore
+    noticed by its neighbours on the host, before they launch a step kernel
+    that would wait for it or write into its freed receive window.  The
+    check costs a few store round trips per step, so it is for runs that
+    need failure detection, not for the timed loop."""
+
+    def __init__(self, halo: Halo, store=None, prefix="dia_hb", timeout=5.0):
+        import torch.distributed.distributed_c10d as c10d
+        self.halo = halo
+        self.store = store if store is not None else c10d._get_default_store()
+        self.prefix, self.timeout = prefix, float(timeout)
+        self.step = 0
+        self.neighbours = [r for r in (halo.rank - 1, halo.rank + 1) if 0 <= r < halo.world]
+
+    def _key(self, r):
+        return f"{self.prefix}/{r}"
+
+    def beat(self):
+        """Announce the next step and wait (bounded) for the neighbours to
+        announce it too; raises PeerLost otherwise."""
+        import time
+        self.step += 1
+        self.store.set(self._key(self.halo.rank), str(self.step))
+        deadline = time.monotonic() + self.timeout
+        for r in self.neighbours:
+            while True:
+                v = self._read(r)
+                if v == "left":
+                    raise PeerLost(f"rank {r} left before step {self.step}")
+                if v is not None and int(v) >= self.step:
+                    break
+                if time.monotonic() > deadline:
+                    raise PeerLost(f"rank {r} missed its heartbeat for step {self.step}")
+                time.sleep(0.01)
+
+    def _read(self, r):
+        import datetime
+        try:
+            self.store.wait([self._key(r)], datetime.timedelta(milliseconds=50))
+        except Exception:  # noqa: BLE001 - key not there yet
+            return None
+        return self.store.get(self._key(r)).decode()
+
+    def leave(self):
+        """Tell the neighbours this rank takes part in no further step."""
+        self.store.set(self._key(self.halo.rank), "left")

@@ -406,6 +406,13 @@ int dia_dist_status(DiaDist* dist, unsigned int* flags, int clear);
  * in the reference, whose kernels have no waits. */
 enum { DIA_TC_TIMEOUT = 1 };
 int dia_device_status(unsigned int* flags, int clear);
+/* Test hook of the tcgen05 dense-band kernel (current device): wait_ns sets
+ * the limit of each of its waits (0: the default of 2 s); withhold != 0
+ * makes one warp of its first CTA skip one arrival, so a wait is certain to
+ * run out and the kernel's abort path (stop, drain issued copies and MMAs,
+ * free tensor memory, set DIA_TC_TIMEOUT) runs.  Both persist until the
+ * next call; reset with (0, 0).  Not for production use. */
+int dia_test_tc_wait(uint64_t wait_ns, int withhold);
 
 /* ------------------------------------------------ synthetic test inputs */
 

@@ -100,3 +100,68 @@ def test_missing_peer_is_reported_not_hung():
             p.kill()
     assert rank == 0 and res.startswith("error"), res
     assert ps[1].exitcode == 7
+
+
+def _hb_worker(rank, world, port, mode, q):
+    """Three ranks step with heartbeats; rank 1 leaves after two steps
+    (announced, or silently).  Ranks 0 and 2 must raise PeerLost before
+    their third step's launch instead of waiting on rank 1."""
+    import datetime
+    from diagpu_b200.dist import Heartbeat, PeerLost
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=20))
+    h = Halo(3000, world, rank, -30, 30)
+    hb = Heartbeat(h, timeout=2.0)
+    ext = torch.zeros(h.width)
+    done = 0
+    try:
+        for step in range(4):
+            if rank == 1 and step == 2:
+                # between steps: its last exchange has been delivered
+                # (neighbours finished step 1) before it goes
+                import time
+                time.sleep(1.0)
+                if mode == "announced":
+                    hb.leave()
+                q.put((rank, "left", done))
+                q.close()
+                q.join_thread()
+                os._exit(0)
+            hb.beat()
+            h.start(ext).wait(timeout=datetime.timedelta(seconds=20))
+            done += 1
+        q.put((rank, "no error", done))
+    except PeerLost as e:
+        q.put((rank, "PeerLost: " + str(e), done))
+    except Exception as e:  # noqa: BLE001 - reported to the test as a failure
+        q.put((rank, "other error: " + repr(e)[:200], done))
+    q.close()
+    q.join_thread()   # flush before the hard exit below
+    if rank == 0:
+        import time
+        time.sleep(3.0)   # rank 0 hosts the store the others are still reading
+    os._exit(0)
+
+
+@pytest.mark.parametrize("mode", ["announced", "silent"])
+def test_heartbeat_reports_a_rank_that_left_between_steps(mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_hb_worker, args=(r, 3, port, mode, q)) for r in range(3)]
+    for p in ps:
+        p.start()
+    res = {}
+    for _ in range(3):
+        r, msg, done = q.get(timeout=120)
+        res[r] = (msg, done)
+    for p in ps:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert res[1][0] == "left"
+    for r in (0, 2):
+        assert res[r][0].startswith("PeerLost"), res
+        assert res[r][1] == 2, res     # both full steps ran; the third never launched

@@ -131,3 +131,33 @@ def test_tcgen05_rejects_wide_bands_auto_falls_back():
     dg.gemm_diag(DA, DA, dev(off), dev(off), n, C, dev(co), dev(cl), dev(k2i), beta=0)
     ref = oracle.gemm_diag(DA.cpu().numpy(), off, DA.cpu().numpy(), off, n, f64=False)[0]
     assert same(C.cpu().numpy(), ref)   # AUTO took the exact SIMT path
+
+
+def test_tcgen05_wait_runs_out_and_the_gpu_stays_usable():
+    """Failure detection without a fault: with a 1 ms wait limit and one
+    operand-ready arrival withheld, the tcgen05 kernel's MMA issuer gives up,
+    every role stops, issued copies drain, tensor memory is freed and
+    DIA_TC_TIMEOUT is reported.  The next normal call is correct."""
+    n = 4096
+    off = np.arange(-4, 5, dtype=np.int32)
+    DA = dg.DiaRows.synth(n, n, off, seed=21).vals[:, :n].contiguous()
+    DB = dg.DiaRows.synth(n, n, off, seed=22).vals[:, :n].contiguous()
+    co, cl, k2i, kl, tot = oracle.build_c_layout(n, off, off)
+    L = dg.lib()
+    dg.device_status(clear=True)
+    C = torch.zeros(tot, device="cuda")
+    dg.check(L.dia_test_tc_wait(1_000_000, 1))
+    try:
+        dg.gemm_diag(DA, DB, dev(off), dev(off), n, C, dev(co), dev(cl), dev(k2i),
+                     mode=dg.GEMM_TCGEN05, beta=0)
+        torch.cuda.synchronize()
+    finally:
+        dg.check(L.dia_test_tc_wait(0, 0))
+    assert dg.device_status(clear=True) & dg.DIA_TC_TIMEOUT
+    C.zero_()
+    dg.gemm_diag(DA, DB, dev(off), dev(off), n, C, dev(co), dev(cl), dev(k2i),
+                 mode=dg.GEMM_TCGEN05, beta=0)
+    torch.cuda.synchronize()
+    assert dg.device_status() == 0
+    ref = oracle.gemm_diag(DA.cpu().numpy(), off, DB.cpu().numpy(), off, n, f64=True)[0]
+    assert rel_l2(C.cpu().numpy(), ref) <= TF32_TOL
