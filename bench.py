@@ -123,7 +123,9 @@ class Clocks:
 def timed(fn, steps, warmup, *, flush=None, per_launch=False, world=1):
     """Mean ms of fn() over `steps` after `warmup`, CUDA events on the
     current stream; with per_launch each call is bracketed by its own events
-    and preceded by flush() (outside the bracket).  With world > 1 a barrier
+    and preceded by flush() and a ~50 us device sleep (both outside the
+    bracket; the sleep keeps the GPU busy while the host enqueues the
+    bracket, so the host's launch latency does not land inside it).  With world > 1 a barrier
     precedes the timed region, so a step that exchanges halos does not start
     its clock while the peer rank is still setting up."""
     for _ in range(warmup):
@@ -134,6 +136,9 @@ def timed(fn, steps, warmup, *, flush=None, per_launch=False, world=1):
         for _ in range(steps):
             if flush is not None:
                 flush()
+            # keep the GPU busy while the host enqueues the bracket, so the
+            # bracket holds device time only, not the host's launch latency
+            torch.cuda._sleep(100_000)
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
             fn()

@@ -170,7 +170,8 @@ struct SumArgs {
     int row_lo;
     int row_hi;
     int ntiles;
-    int tiles_per_item;  /* consecutive row tiles one work item covers */
+    int tiles_per_item;  /* consecutive row tiles one work item covers; 0: chosen
+                          * on the device from the term counts in outs */
     const int* nOut_dev; /* optional device-resident count; nOut is then a capacity */
 };
 
@@ -184,6 +185,23 @@ __global__ void __launch_bounds__(kBlock) pair_sum_kernel(SumArgs s)
     constexpr int kTile = kBlock * ILP;
     __shared__ Term s_t[kMaxTerms];
     const int nOut = s.nOut_dev ? min(*s.nOut_dev, s.nOut) : s.nOut;
+    if (s.tiles_per_item == 0) {
+        /* the host could not see the plan: every CTA sums the term counts
+         * (a few thousand descriptors at most, L2-resident) and applies the
+         * host rule of launch_pair_sum_t */
+        __shared__ long long s_terms;
+        if (threadIdx.x == 0) s_terms = 0;
+        __syncthreads();
+        long long mine = 0;
+        for (int c = threadIdx.x; c < nOut; c += kBlock) mine += s.outs[c].t1 - s.outs[c].t0;
+        atomicAdd((unsigned long long*)&s_terms, (unsigned long long)mine);
+        __syncthreads();
+        const long long tiles = (long long)nOut * s.ntiles;
+        int tpi = 1;
+        if (s_terms <= 2LL * nOut)
+            tpi = (int)max(1LL, min(16LL, tiles / (8LL * gridDim.x)));
+        s.tiles_per_item = tpi;
+    }
     const int nchunks = (s.ntiles + s.tiles_per_item - 1) / s.tiles_per_item;
     const long long items = (long long)nOut * nchunks;
     for (long long it = blockIdx.x; it < items; it += gridDim.x) {
@@ -259,8 +277,15 @@ static int launch_pair_sum_t(const float* U, const float* V, float* O, const Out
     s.tiles_per_item = 1;
     if (avg_terms >= 0.0f && avg_terms <= 2.0f)
         s.tiles_per_item = (int)std::max(1LL, std::min(16LL, tiles / (8 * slots)));
-    const int nchunks = (s.ntiles + s.tiles_per_item - 1) / s.tiles_per_item;
-    const long long grid = std::min(slots, (long long)nOut * nchunks);
+    long long grid;
+    if (avg_terms < 0.0f && nOut_dev == nullptr) {
+        /* term counts unknown on the host (device-planned products) */
+        s.tiles_per_item = 0;
+        grid = std::min(slots, tiles);
+    } else {
+        const int nchunks = (s.ntiles + s.tiles_per_item - 1) / s.tiles_per_item;
+        grid = std::min(slots, (long long)nOut * nchunks);
+    }
     if (accumulate)
         pair_sum_kernel<true, ILP, BATCH><<<(unsigned)grid, kBlock, 0, stream>>>(s);
     else
