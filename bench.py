@@ -859,6 +859,16 @@ def _only_spmv(dg, n, offs):
     return (lambda: dg.spmv(A, x, y)), spmv_bytes(n, offs, 0, n)[0]
 
 
+def _only_spmv_block(dg, world=8, rank=1):
+    """The plain block kernel on the same rank block as spmv5_peer."""
+    from diagpu_b200.dist import Halo
+    h = Halo(N5, world, rank, int(OFF5.min()), int(OFF5.max()))
+    A = dg.DiaRows.synth(N5, N5, OFF5, SEED_A, vrow0=h.r0, nrows=h.r1 - h.r0)
+    xe = dg.synth_vector(h.xhi - h.xlo, SEED_X, i0=h.xlo)
+    y = torch.empty(A.stride, device="cuda")
+    return (lambda: dg.spmv(A, xe, y, x_lo=h.xlo)), spmv_bytes(N5, OFF5, h.r0, h.r1)[0]
+
+
 def _only_spmspm(dg, n, offsA, offsB=None, kind=0):
     A = dg.DiaRows.synth(n, n, offsA, SEED_A, kind=kind, lo=-1.0 if kind == 0 else 0.0)
     B = A if offsB is None else dg.DiaRows.synth(n, n, offsB, SEED_X, kind=kind,
@@ -976,12 +986,54 @@ def _only_chain(dg, host=False, n=1 << 20, k=CHAIN_K):
     return fn, chain_bytes(n, CHAIN_OFF, k)
 
 
+def _only_peer(dg, world=8, rank=1):
+    """The fused peer-halo step kernel on one GPU: rank `rank` of `world`
+    on config 5, its neighbours emulated by local buffers and its flags set
+    far ahead, so no launch waits for another (for ncu captures)."""
+    import ctypes as C
+    from diagpu_b200.dist import Halo, PeerHalo, spmv_rows_peer
+    h = Halo(N5, world, rank, int(OFF5.min()), int(OFF5.max()))
+    A = dg.DiaRows.synth(N5, N5, OFF5, SEED_A, vrow0=h.r0, nrows=h.r1 - h.r0)
+    x = dg.synth_vector(N5, SEED_X)
+    x_own = x[h.r0:h.r1].clone()
+    rg = h.ranges()
+    keep = [x_own, A]
+    sh = PeerHalo()
+    for q in range(2):
+        lo, hi = x[h.xlo:h.r0].clone(), x[h.r1:h.xhi].clone()
+        pl = torch.zeros(int(rg[3]) - h.r0, device="cuda")
+        pr = torch.zeros(h.r1 - int(rg[6]), device="cuda")
+        keep += [lo, hi, pl, pr]
+        sh.halo_lo[q], sh.halo_hi[q] = lo.data_ptr(), hi.data_ptr()
+        sh.peer_left_halo_hi[q], sh.peer_right_halo_lo[q] = pl.data_ptr(), pr.data_ptr()
+    ctl = torch.zeros(8, dtype=torch.int64, device="cuda")
+    ctl[0] = ctl[1] = 1 << 40
+    pctl = torch.zeros(2, dtype=torch.int64, device="cuda")
+    keep += [ctl, pctl]
+    sh.flag_lo, sh.flag_hi = ctl.data_ptr(), ctl.data_ptr() + 8
+    sh.push_count, sh.status = ctl.data_ptr() + 16, ctl.data_ptr() + 32
+    sh.peer_left_flag_hi, sh.peer_right_flag_lo = pctl.data_ptr() + 8, pctl.data_ptr()
+    sh.send_left_hi, sh.send_right_lo = int(rg[3]), int(rg[6])
+    sh.has_left, sh.has_right = 1, 1
+    sh.timeout_ns = 2_000_000_000
+    y = torch.empty(A.stride, device="cuda")
+    step = [0]
+
+    def fn():
+        step[0] += 1
+        spmv_rows_peer(sh, step[0], A, h.r0, h.r1, h.xlo, h.xhi, x_own, y)
+    fn.keep = keep
+    return fn, spmv_bytes(N5, OFF5, h.r0, h.r1)[0]
+
+
 # name -> builder(dg) returning (callable, algorithmic bytes); the "_s" cases
 # are reduced sizes (<= a few GB on the device) for ncu captures
 ONLY = {
     "spmv5": lambda dg: _only_spmv(dg, N5, OFF5),
     "spmv5_s": lambda dg: _only_spmv(dg, 256 * 256 * 64, OFF5),
     "spmv1": lambda dg: _only_spmv(dg, 1 << 20, np.array([-1024, -1, 0, 1, 1024], np.int32)),
+    "spmv5_peer": lambda dg: _only_peer(dg),
+    "spmv5_block8": lambda dg: _only_spmv_block(dg),
     "spmspm5": lambda dg: _only_spmspm(dg, N5, OFF5),
     "spmspm5_s": lambda dg: _only_spmspm(dg, 256 * 256 * 64, OFF5),
     "spmspm2": lambda dg: _only_spmspm(dg, 128 ** 3, np.array([-16384, -128, -1, 0, 1, 128,
