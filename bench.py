@@ -587,6 +587,35 @@ def run_ours(args):
     dm = DistSpmspm(A, B_ext, halo)
     ksp = max(3, min(K, 10))
     mm_ms = max_over_ranks(timed(lambda: dm.step(), ksp, max(1, min(W, 3)), world=world), world)
+    # breakdown of one partitioned C = A*A step: interior rows (own B rows
+    # only), boundary rows, and at N > 1 the B halo exchange alone
+    mw = max(1, min(W, 3))
+    ia, ib = halo.interior()
+    mm_break = {"step_ms": round(mm_ms, 4)}
+    if ib > ia:
+        plan_in = dm.plan_own if world > 1 else dm.plan_all
+        mm_break["interior_ms"] = round(max_over_ranks(timed(
+            lambda: plan_in.execute(A, dm.B, dm.C, ia, ib), ksp, mw, world=world), world), 4)
+    bnd = halo.boundary()
+    if world > 1:
+        def bonly():
+            for lo, hi in bnd:
+                dm.plan_all.execute(A, dm.B, dm.C, lo, hi)
+        mm_break["boundary_ms"] = round(max_over_ranks(timed(bonly, ksp, mw, world=world),
+                                                       world), 4)
+        if dm.native is not None:
+            from diagpu_b200 import _stream, check, lib
+            import ctypes as C
+            rgm = halo.ranges()
+
+            def honly():
+                check(lib().dia_dist_halo_start(dm.native.handle, dg._dptr(dm.B.vals),
+                                                dm.B.vrow0, dm.B.stride, dm.B.K,
+                                                rgm.ctypes.data_as(C.c_void_p), _stream()))
+                check(lib().dia_dist_halo_wait(dm.native.handle, _stream()))
+            mm_break["halo_alone_ms"] = round(max_over_ranks(timed(honly, ksp, mw, world=world),
+                                                             world), 4)
+        mm_break["boundary_rows"] = sum(hi - lo for lo, hi in bnd)
     sym = dm.sym
     fl = spmspm_useful(N5, OFF5, OFF5, sym, 0, N5)
     nnzC = int(sym["C_len"].astype(np.int64).sum())
@@ -604,7 +633,7 @@ def run_ours(args):
     spmspm5 = {"workload": "config5 C=A*A (125 output diagonals, 729 pairs)",
                "metric": "spmspm_useful_GFLOPs", "value": round(fl / mm_ms / 1e6, 2),
                "unit": "GFLOP/s", "ms": round(mm_ms, 4), "GBps": round(mm_bytes / mm_ms / 1e6, 1),
-               "bytes": mm_bytes, "useful_flops": fl, "n_gpus": world,
+               "bytes": mm_bytes, "useful_flops": fl, "n_gpus": world, "breakdown": mm_break,
                "roofline": roofline(rank_mm_bytes / mm_ms / 1e6, hbm, src)}
     del dm, A
     torch.cuda.empty_cache()

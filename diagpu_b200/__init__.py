@@ -27,7 +27,7 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libdiagpu_b200.so")
 
-DIA_OK, DIA_ERR_INVALID, DIA_ERR_CUDA, DIA_ERR_UNSUPPORTED, DIA_ERR_CAPACITY = range(5)
+DIA_OK, DIA_ERR_INVALID, DIA_ERR_CUDA, DIA_ERR_UNSUPPORTED, DIA_ERR_CAPACITY, DIA_ERR_TIMEOUT = range(6)
 DIA_TC_TIMEOUT = 1   # dia_device_status bit: a tcgen05 kernel wait ran out
 GEMM_AUTO, GEMM_SIMT, GEMM_TCGEN05 = 0, 1, 2
 ALIGN = 32  # floats per stride unit (128 bytes)
@@ -71,6 +71,8 @@ def lib():
             getattr(L, name).restype = i
         L.dia_nccl_unique_id.argtypes = [p, i]
         L.dia_dist_create.argtypes = [i, i, p, p]
+        L.dia_dist_create_timeout.argtypes = [i, i, p, i64, p]
+        L.dia_dist_abort.argtypes = [p]
         L.dia_dist_halo_start.argtypes = [p, p, i64, i64, i, p, p]
         L.dia_dist_halo_wait.argtypes = [p, p]
         L.dia_dist_spmv_step.argtypes = [p, i64, i64, i, p, p, i64, i64, p, i64, i64, p, p, i64,
@@ -85,7 +87,8 @@ def lib():
         L.dia_dist_status.argtypes = [p, p, i]
         for name in ("dia_nccl_unique_id", "dia_dist_create", "dia_dist_halo_start",
                      "dia_dist_halo_wait", "dia_dist_spmv_step", "dia_dist_async_error",
-                     "dia_dist_destroy", "dia_spmv_rows_peer", "dia_dist_peer_setup",
+                     "dia_dist_destroy", "dia_dist_create_timeout", "dia_dist_abort",
+                     "dia_spmv_rows_peer", "dia_dist_peer_setup",
                      "dia_dist_spmv_fused", "dia_dist_set_timeout", "dia_dist_status"):
             getattr(L, name).restype = i
         L.dia_device_status.argtypes = [p, i]

@@ -23,8 +23,10 @@
  */
 #include <nccl.h>
 
+#include <chrono>
 #include <cstring>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "../../include/diagpu_b200.h"
@@ -42,6 +44,7 @@ struct DiaDist {
     uint64_t step = 0;
     int64_t r0 = 0, r1 = 0, x_lo = 0, x_hi = 0;
     bool peer_ready = false;
+    int64_t comm_timeout_ms = 120000;   /* deadline of each host-side NCCL completion */
 };
 
 namespace {
@@ -56,6 +59,51 @@ int nccl_fail(ncclResult_t r, const char* what)
         ncclResult_t r__ = (expr);                          \
         if (r__ != ncclSuccess) return nccl_fail(r__, #expr); \
     } while (0)
+
+/* The communicator is non-blocking: a call may return ncclInProgress while
+ * NCCL finishes it in the background (connection set-up, init bootstrap).
+ * Completion is polled here against a deadline; a communicator that does
+ * not complete in time (a rank that never joined, a peer that stopped
+ * answering during set-up) is aborted and the call returns DIA_ERR_TIMEOUT,
+ * instead of the process blocking forever.  Only host-side completion is
+ * covered: a transfer that the GPU has started waits on the GPU, which is
+ * why ranks check each other on the host before every step. */
+int nccl_complete(DiaDist* d, ncclResult_t r, const char* what)
+{
+    if (r == ncclSuccess) return DIA_OK;
+    if (r != ncclInProgress) return nccl_fail(r, what);
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        ncclResult_t st = ncclSuccess;
+        const ncclResult_t q = ncclCommGetAsyncError(d->comm, &st);
+        if (q != ncclSuccess) return nccl_fail(q, what);
+        if (st == ncclSuccess) return DIA_OK;
+        if (st != ncclInProgress) return nccl_fail(st, what);
+        const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
+                            std::chrono::steady_clock::now() - t0).count();
+        if (ms > d->comm_timeout_ms) {
+            ncclCommAbort(d->comm);
+            d->comm = nullptr;
+            return dia::fail(DIA_ERR_TIMEOUT, std::string(what) + ": not complete after " +
+                                             std::to_string(d->comm_timeout_ms) +
+                                             " ms; communicator aborted");
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
+#define DIA_NCCL_DONE(d, expr)                                      \
+    do {                                                            \
+        const int rc__ = nccl_complete((d), (expr), #expr);          \
+        if (rc__ != DIA_OK) return rc__;                            \
+    } while (0)
+
+int need_comm(const DiaDist* d, const char* who)
+{
+    if (!d) return dia::fail(DIA_ERR_INVALID, std::string(who) + ": null handle");
+    if (!d->comm) return dia::fail(DIA_ERR_INVALID, std::string(who) + ": communicator was aborted");
+    return DIA_OK;
+}
 
 /* ranges: recv-left [0,1), send-left [2,3), recv-right [4,5), send-right
  * [6,7) as global column indices; ext column j holds global column
@@ -78,7 +126,7 @@ int halo_post(DiaDist* d, float* ext, int64_t ext_lo, int64_t pitch, int K,
                                       d->cs));
         }
     }
-    DIA_TRY_NCCL(ncclGroupEnd());
+    DIA_NCCL_DONE(d, ncclGroupEnd());
     return DIA_OK;
 }
 
@@ -96,20 +144,26 @@ extern "C" int dia_nccl_unique_id(void* out, int nbytes)
     return DIA_OK;
 }
 
-extern "C" int dia_dist_create(int rank, int world, const void* id, DiaDist** out)
+extern "C" int dia_dist_create_timeout(int rank, int world, const void* id, int64_t timeout_ms,
+                                       DiaDist** out)
 {
-    if (!out || !id || world < 1 || rank < 0 || rank >= world)
-        return fail(DIA_ERR_INVALID, "dia_dist_create: bad rank/world or null pointer");
+    if (!out || !id || world < 1 || rank < 0 || rank >= world || timeout_ms <= 0)
+        return fail(DIA_ERR_INVALID, "dia_dist_create: bad rank/world/timeout or null pointer");
     *out = nullptr;
     auto* d = new DiaDist();
     d->rank = rank;
     d->world = world;
+    d->comm_timeout_ms = timeout_ms;
     ncclUniqueId uid;
     std::memcpy(&uid, id, sizeof(uid));
-    ncclResult_t r = ncclCommInitRank(&d->comm, world, uid, rank);
-    if (r != ncclSuccess) {
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    const int rc0 = nccl_complete(d, ncclCommInitRankConfig(&d->comm, world, uid, rank, &cfg),
+                                  "ncclCommInitRankConfig");
+    if (rc0 != DIA_OK) {
+        if (d->comm) ncclCommAbort(d->comm);
         delete d;
-        return nccl_fail(r, "ncclCommInitRank");
+        return rc0;
     }
     /* the halo stream gets the highest priority: its small kernels (NCCL's,
      * the boundary strips) are then dispatched ahead of the interior
@@ -120,11 +174,24 @@ extern "C" int dia_dist_create(int rank, int world, const void* id, DiaDist** ou
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&d->ready, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&d->done, cudaEventDisableTiming);
     if (e != cudaSuccess) {
-        ncclCommDestroy(d->comm);
+        ncclCommAbort(d->comm);
         delete d;
         return cuda_fail(e, "dia_dist_create stream/events");
     }
     *out = d;
+    return DIA_OK;
+}
+
+extern "C" int dia_dist_create(int rank, int world, const void* id, DiaDist** out)
+{
+    return dia_dist_create_timeout(rank, world, id, 120000, out);
+}
+
+extern "C" int dia_dist_abort(DiaDist* d)
+{
+    if (!d) return fail(DIA_ERR_INVALID, "dia_dist_abort: null handle");
+    if (d->comm) ncclCommAbort(d->comm);
+    d->comm = nullptr;
     return DIA_OK;
 }
 
@@ -133,6 +200,7 @@ extern "C" int dia_dist_halo_start(DiaDist* d, float* d_ext, int64_t ext_lo, int
 {
     if (!d || !d_ext || !h_ranges || K < 0)
         return fail(DIA_ERR_INVALID, "dia_dist_halo_start: null pointer or bad K");
+    if (int rc = need_comm(d, "dia_dist_halo_start")) return rc;
     DIA_TRY_CUDA(cudaEventRecord(d->ready, stream));
     DIA_TRY_CUDA(cudaStreamWaitEvent(d->cs, d->ready, 0));
     const int rc = halo_post(d, d_ext, ext_lo, pitch, K, h_ranges);
@@ -155,7 +223,7 @@ extern "C" int dia_dist_spmv_step(DiaDist* d, int64_t n_rows, int64_t n_cols, in
                                   int64_t int_lo, int64_t int_hi, int overlap,
                                   cudaStream_t stream)
 {
-    if (!d) return fail(DIA_ERR_INVALID, "dia_dist_spmv_step: null handle");
+    if (int rc0 = need_comm(d, "dia_dist_spmv_step")) return rc0;
     int rc = DIA_OK;
     if (!overlap) {
         /* exchange first, then one launch over the whole block: the halo is
@@ -213,7 +281,7 @@ extern "C" int dia_dist_spmv_step(DiaDist* d, int64_t n_rows, int64_t n_cols, in
 
 extern "C" int dia_dist_async_error(DiaDist* d)
 {
-    if (!d) return fail(DIA_ERR_INVALID, "dia_dist_async_error: null handle");
+    if (int rc = need_comm(d, "dia_dist_async_error")) return rc;
     ncclResult_t ar = ncclSuccess;
     DIA_TRY_NCCL(ncclCommGetAsyncError(d->comm, &ar));
     if (ar != ncclSuccess && ar != ncclInProgress) return nccl_fail(ar, "NCCL async error");
@@ -232,7 +300,13 @@ extern "C" int dia_dist_destroy(DiaDist* d)
             if (p) cudaIpcCloseMemHandle(p);
         cudaFree(d->window);
     }
-    if (d->comm) ncclCommDestroy(d->comm);
+    if (d->comm) {
+        /* non-blocking: finalize completes in the background, then destroy */
+        if (nccl_complete(d, ncclCommFinalize(d->comm), "ncclCommFinalize") == DIA_OK && d->comm)
+            ncclCommDestroy(d->comm);
+        else if (d->comm)
+            ncclCommAbort(d->comm);
+    }
     if (d->ready) cudaEventDestroy(d->ready);
     if (d->done) cudaEventDestroy(d->done);
     if (d->cs) cudaStreamDestroy(d->cs);
@@ -274,6 +348,7 @@ extern "C" int dia_dist_peer_setup(DiaDist* d, int64_t r0, int64_t r1, int64_t x
                                    const int64_t* rg)
 {
     if (!d || !rg) return fail(DIA_ERR_INVALID, "dia_dist_peer_setup: null pointer");
+    if (int rc = need_comm(d, "dia_dist_peer_setup")) return rc;
     if (d->window) return fail(DIA_ERR_INVALID, "dia_dist_peer_setup: already set up");
     if (x_lo > r0 || x_hi < r1 || r1 < r0)
         return fail(DIA_ERR_INVALID, "dia_dist_peer_setup: inconsistent halo window");
@@ -291,15 +366,17 @@ extern "C" int dia_dist_peer_setup(DiaDist* d, int64_t r0, int64_t r1, int64_t x
     PeerInfo* dbuf = nullptr;
     DIA_TRY_CUDA(cudaMalloc(&dbuf, sizeof(PeerInfo) * (size_t)(d->world + 1)));
     DIA_TRY_CUDA(cudaMemcpy(dbuf + d->world, &mine, sizeof(mine), cudaMemcpyHostToDevice));
-    ncclResult_t nr = ncclAllGather(dbuf + d->world, dbuf, sizeof(PeerInfo), ncclChar, d->comm,
-                                    d->cs);
+    const int grc = nccl_complete(d, ncclAllGather(dbuf + d->world, dbuf, sizeof(PeerInfo),
+                                                   ncclChar, d->comm, d->cs),
+                                  "dia_dist_peer_setup: ncclAllGather");
+    const ncclResult_t nr = grc == DIA_OK ? ncclSuccess : ncclInternalError;
     std::vector<PeerInfo> all((size_t)d->world);
     if (nr == ncclSuccess) e = cudaStreamSynchronize(d->cs);
     if (nr == ncclSuccess && e == cudaSuccess)
         e = cudaMemcpy(all.data(), dbuf, sizeof(PeerInfo) * (size_t)d->world,
                        cudaMemcpyDeviceToHost);
     cudaFree(dbuf);
-    if (nr != ncclSuccess) return nccl_fail(nr, "dia_dist_peer_setup: ncclAllGather");
+    if (grc != DIA_OK) return grc;
     if (e != cudaSuccess) return cuda_fail(e, "dia_dist_peer_setup: handle exchange");
     for (const PeerInfo& pi : all)
         if (!pi.valid)
@@ -356,10 +433,11 @@ extern "C" int dia_dist_peer_setup(DiaDist* d, int64_t r0, int64_t r1, int64_t x
     DIA_TRY_CUDA(cudaDeviceSynchronize());
     int* one = nullptr;
     DIA_TRY_CUDA(cudaMalloc(&one, sizeof(int)));
-    nr = ncclAllReduce(one, one, 1, ncclInt, ncclSum, d->comm, d->cs);
-    if (nr == ncclSuccess) e = cudaStreamSynchronize(d->cs);
+    const int brc = nccl_complete(d, ncclAllReduce(one, one, 1, ncclInt, ncclSum, d->comm, d->cs),
+                                  "dia_dist_peer_setup: barrier");
+    if (brc == DIA_OK) e = cudaStreamSynchronize(d->cs);
     cudaFree(one);
-    if (nr != ncclSuccess) return nccl_fail(nr, "dia_dist_peer_setup: barrier");
+    if (brc != DIA_OK) return brc;
     if (e != cudaSuccess) return cuda_fail(e, "dia_dist_peer_setup: barrier");
     d->peer_ready = true;
     return DIA_OK;

@@ -36,7 +36,8 @@ enum {
     DIA_ERR_INVALID = 1,     /* bad argument (sizes, null pointers, layout) */
     DIA_ERR_CUDA = 2,        /* a CUDA runtime call or launch failed */
     DIA_ERR_UNSUPPORTED = 3, /* valid input outside what this build handles */
-    DIA_ERR_CAPACITY = 4     /* caller buffer too small (two-call pattern) */
+    DIA_ERR_CAPACITY = 4,    /* caller buffer too small (two-call pattern) */
+    DIA_ERR_TIMEOUT = 5      /* a peer did not complete in time; communicator aborted */
 };
 
 /* Message for the last failing call on this host thread ("" if none). */
@@ -318,6 +319,18 @@ int dia_gemm_diag_ex(const float* d_DA, const float* d_DB, const int* d_off_A,
 typedef struct DiaDist DiaDist;
 int dia_nccl_unique_id(void* h_id, int nbytes);
 int dia_dist_create(int rank, int world, const void* h_id, DiaDist** dist);
+/* dia_dist_create with a deadline.  The communicator is non-blocking: its
+ * init and every later call that NCCL completes in the background are
+ * polled until timeout_ms; a rank that never joins (or stops answering
+ * during set-up) makes the call abort the communicator and return
+ * DIA_ERR_TIMEOUT instead of blocking forever.  dia_dist_create uses 120 s.
+ * Transfers already running on the GPU are not covered: ranks must learn of
+ * a departed peer on the host before their next step. */
+int dia_dist_create_timeout(int rank, int world, const void* h_id, int64_t timeout_ms,
+                            DiaDist** dist);
+/* Abort the communicator (ncclCommAbort); later calls on it fail with
+ * DIA_ERR_INVALID.  dia_dist_destroy still frees the handle. */
+int dia_dist_abort(DiaDist* dist);
 /* Exchange halo columns of a [K rows x pitch] buffer whose column j holds
  * global column ext_lo + j.  h_ranges (8 x int64, global columns): receive
  * from rank-1 [0,1), send to rank-1 [2,3), receive from rank+1 [4,5), send
