@@ -10,13 +10,21 @@
  *     C[alpha+beta+s][i] += sum_{u+v=s} A[alpha+u][i] * B[beta+v][i+alpha+u].
  * When run pairs with different alpha+beta never overlap, the outputs split
  * into blocks of W diagonals, each fed by a list of run pairs.  A thread
- * then owns 4 consecutive rows of one block: W x 4 accumulators in
- * registers, the P x 4 A values of a run pair loaded once (float4), and for
- * each B diagonal of the run one aligned 12-value window (three float4
- * loads) that serves all P shifted uses.  Every register index is a
- * compile-time constant (the window's alignment shift is a uniform switch).
- * That is about 2.5 instructions per product instead of the ~10 of the
- * generic pair-sum kernel.
+ * owns R consecutive rows of one block (R = 8 for runs of 2 or 3, 4 for
+ * longer runs): W x R accumulators in registers and the P x R A values of a
+ * run pair, loaded as one aligned R-float vector per diagonal.
+ *
+ * The B values a thread needs for one B diagonal are the R + P - 1
+ * consecutive rows i+alpha .. i+alpha+R+P-2: a window that starts D rows
+ * into an aligned R-row chunk and spills into the next chunk (or two).  The
+ * lanes of a warp own consecutive chunks, so each lane loads only one
+ * aligned chunk (one fully coalesced vector load for the warp) and takes
+ * the few values that lie in its neighbours' chunks with warp shuffles; the
+ * lanes at the warp's two ends load the chunk past the warp themselves.
+ * Loading overlapping windows instead moved 2-3 times the bytes through
+ * the L1 data pipe, which bounded the kernel there (ncu: L1 at 93-97 % of
+ * peak with DRAM at 28-37 %).  D is uniform per run pair, so every register
+ * index is a compile-time constant (a uniform switch over D).
  *
  * Summation order: the run pairs of a block are sorted by alpha, and inside
  * a pair u ascends, so every output accumulates its terms in ascending A
@@ -35,12 +43,19 @@
 namespace dia {
 
 constexpr int kRpThreads = 256;
-constexpr int kRpRows = kRpThreads * 4;   /* rows per tile */
+
+/* rows per thread: 8 for runs of 2 or 3, 4 for longer runs (registers) */
+template <int P>
+struct RpRows {
+    static constexpr int value = P <= 3 ? 8 : 4;
+};
+template <int P>
+__host__ __device__ constexpr int rp_tile_rows() { return kRpThreads * RpRows<P>::value; }
 
 struct RunPairDesc {
     long long a_elem;   /* A element offset of (first A diagonal of the run, row 0) */
     long long b_elem;   /* B element offset of (first B diagonal, row 0) + alpha - shift */
-    int shift;          /* (row + alpha - b_vrow0) mod 4 at tile-aligned rows */
+    int shift;          /* (row + alpha - b_vrow0) mod R at tile-aligned rows */
     int pad;
 };
 
@@ -59,66 +74,157 @@ struct RpArgs {
     int nblk, i_lo, ntiles;
 };
 
-template <int P, int Q, int NL, int S>
-__device__ __forceinline__ void rp_body(float (&acc)[P + Q - 1][4], const float (&a)[P][4],
-                                        const float (&raw)[Q][4 * NL])
+/* aligned R-float vector load (read-only path) and streaming store */
+template <int R>
+__device__ __forceinline__ void vload(float (&r)[R], const float* p);
+template <>
+__device__ __forceinline__ void vload<4>(float (&r)[4], const float* p)
 {
+    const float4 x = __ldg((const float4*)p);
+    r[0] = x.x; r[1] = x.y; r[2] = x.z; r[3] = x.w;
+}
+template <>
+__device__ __forceinline__ void vload<8>(float (&r)[8], const float* p)
+{
+    asm volatile("ld.global.nc.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=f"(r[0]), "=f"(r[1]), "=f"(r[2]), "=f"(r[3]), "=f"(r[4]), "=f"(r[5]),
+                   "=f"(r[6]), "=f"(r[7])
+                 : "l"(p));
+}
+template <int R>
+__device__ __forceinline__ void vstore_cs(float* p, const float (&r)[R]);
+template <>
+__device__ __forceinline__ void vstore_cs<4>(float* p, const float (&r)[4])
+{
+    __stcs((float4*)p, make_float4(r[0], r[1], r[2], r[3]));
+}
+template <>
+__device__ __forceinline__ void vstore_cs<8>(float* p, const float (&r)[8])
+{
+    asm volatile("st.global.cs.v8.f32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
+                 ::"l"(p), "f"(r[0]), "f"(r[1]), "f"(r[2]), "f"(r[3]), "f"(r[4]), "f"(r[5]),
+                   "f"(r[6]), "f"(r[7])
+                 : "memory");
+}
+
+/* Window positions [D, D+L) relative to the aligned chunk start; chunk
+ * q = p / R.  The lane loads chunk `own` and shuffles the rest in: pick the
+ * chunk that leaves the fewest positions outside it. */
+__host__ __device__ constexpr int rp_outside(int D, int L, int R, int c)
+{
+    int n = 0;
+    for (int p = D; p < D + L; ++p) n += (p / R != c);
+    return n;
+}
+__host__ __device__ constexpr int rp_own(int D, int L, int R)
+{
+    int best = 0;
+    for (int c = 1; c <= (D + L - 1) / R; ++c)
+        if (rp_outside(D, L, R, c) < rp_outside(D, L, R, best)) best = c;
+    return best;
+}
+
+/* One run pair on R consecutive rows.  bp points at B row (i + alpha - D)
+ * of the run's first B diagonal, an aligned chunk start. */
+template <int P, int Q, int R, int D>
+__device__ __forceinline__ void rp_body(float (&acc)[P + Q - 1][R], const float (&a)[P][R],
+                                        const float* __restrict__ bp, long long B_stride,
+                                        int lane)
+{
+    constexpr int L = P + R - 1;                 /* window length */
+    constexpr int NQ = (D + L - 1) / R + 1;      /* chunks the window touches */
+    constexpr int OWN = rp_own(D, L, R);
+    float w[Q][L];
+#pragma unroll
+    for (int v = 0; v < Q; ++v) {
+        const float* cp = bp + v * B_stride;
+        float own[R];
+        vload<R>(own, cp + OWN * R);
+#pragma unroll
+        for (int q = 0; q < NQ; ++q) {
+            if (q == OWN) {
+#pragma unroll
+                for (int p = D; p < D + L; ++p)
+                    if (p / R == q) w[v][p - D] = own[p % R];
+                continue;
+            }
+            /* lanes whose neighbour lane + (q - OWN) lies outside the warp
+             * load that chunk themselves */
+            const int src = lane + (q - OWN);
+            const bool outside = src < 0 || src > 31;
+            float fx[R];
+#pragma unroll
+            for (int k = 0; k < R; ++k) fx[k] = 0.0f;
+            if (outside) vload<R>(fx, cp + q * R);
+#pragma unroll
+            for (int p = D; p < D + L; ++p)
+                if (p / R == q) {
+                    const float sh = __shfl_sync(0xffffffffu, own[p % R], src & 31);
+                    w[v][p - D] = outside ? fx[p % R] : sh;
+                }
+        }
+    }
 #pragma unroll
     for (int u = 0; u < P; ++u)
 #pragma unroll
         for (int v = 0; v < Q; ++v)
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-                acc[u + v][j] = mul_add_rn(acc[u + v][j], a[u][j], raw[v][S + u + j]);
+            for (int j = 0; j < R; ++j)
+                acc[u + v][j] = mul_add_rn(acc[u + v][j], a[u][j], w[v][u + j]);
+}
+
+template <int P, int Q, int R>
+__device__ __forceinline__ void rp_dispatch(float (&acc)[P + Q - 1][R], const float (&a)[P][R],
+                                            const float* bp, long long B_stride, int lane,
+                                            int D)
+{
+    if (R == 8) {
+        switch (D) {
+            case 0: rp_body<P, Q, R, 0>(acc, a, bp, B_stride, lane); break;
+            case 1: rp_body<P, Q, R, 1>(acc, a, bp, B_stride, lane); break;
+            case 2: rp_body<P, Q, R, 2>(acc, a, bp, B_stride, lane); break;
+            case 3: rp_body<P, Q, R, 3>(acc, a, bp, B_stride, lane); break;
+            case 4: rp_body<P, Q, R, 4 % R>(acc, a, bp, B_stride, lane); break;
+            case 5: rp_body<P, Q, R, 5 % R>(acc, a, bp, B_stride, lane); break;
+            case 6: rp_body<P, Q, R, 6 % R>(acc, a, bp, B_stride, lane); break;
+            default: rp_body<P, Q, R, 7 % R>(acc, a, bp, B_stride, lane); break;
+        }
+    } else {
+        switch (D) {
+            case 0: rp_body<P, Q, R, 0>(acc, a, bp, B_stride, lane); break;
+            case 1: rp_body<P, Q, R, 1>(acc, a, bp, B_stride, lane); break;
+            case 2: rp_body<P, Q, R, 2>(acc, a, bp, B_stride, lane); break;
+            default: rp_body<P, Q, R, 3>(acc, a, bp, B_stride, lane); break;
+        }
+    }
 }
 
 template <int P, int Q>
 __global__ void __launch_bounds__(kRpThreads) runpair_kernel(RpArgs p)
 {
     constexpr int W = P + Q - 1;
-    constexpr int NL = (3 + (P - 1) + 4 + 3) / 4;   /* float4 loads per B window */
+    constexpr int R = RpRows<P>::value;
+    const int lane = threadIdx.x & 31;
     const long long items = (long long)p.nblk * p.ntiles;
     for (long long it = blockIdx.x; it < items; it += gridDim.x) {
         const int k = (int)(it % p.nblk);
-        const long long i = (long long)p.i_lo + (it / p.nblk) * kRpRows + 4 * threadIdx.x;
+        const long long i =
+            (long long)p.i_lo + (it / p.nblk) * rp_tile_rows<P>() + R * threadIdx.x;
         const RunBlock bk = p.blks[k];
-        float acc[W][4];
+        float acc[W][R];
 #pragma unroll
         for (int s = 0; s < W; ++s)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) acc[s][j] = 0.0f;
+            for (int j = 0; j < R; ++j) acc[s][j] = 0.0f;
         for (int r = bk.rp0; r < bk.rp1; ++r) {
             const RunPairDesc d = p.rps[r];
-            float a[P][4];
+            float a[P][R];
 #pragma unroll
-            for (int u = 0; u < P; ++u) {
-                const float4 x = __ldg((const float4*)(p.A + d.a_elem + u * p.A_stride + i));
-                a[u][0] = x.x; a[u][1] = x.y; a[u][2] = x.z; a[u][3] = x.w;
-            }
-            /* L1 wavefronts of these overlapping window loads bound this
-             * kernel (ncu: L1 throughput 93 % of peak on config 5); loading
-             * the last float4 only when the shift needs it measured slower */
-            float raw[Q][4 * NL];
-#pragma unroll
-            for (int v = 0; v < Q; ++v)
-#pragma unroll
-                for (int m = 0; m < NL; ++m) {
-                    const float4 x =
-                        __ldg((const float4*)(p.B + d.b_elem + v * p.B_stride + i + 4 * m));
-                    raw[v][4 * m] = x.x; raw[v][4 * m + 1] = x.y;
-                    raw[v][4 * m + 2] = x.z; raw[v][4 * m + 3] = x.w;
-                }
-            switch (d.shift) {
-                case 0: rp_body<P, Q, NL, 0>(acc, a, raw); break;
-                case 1: rp_body<P, Q, NL, 1>(acc, a, raw); break;
-                case 2: rp_body<P, Q, NL, 2>(acc, a, raw); break;
-                default: rp_body<P, Q, NL, 3>(acc, a, raw); break;
-            }
+            for (int u = 0; u < P; ++u) vload<R>(a[u], p.A + d.a_elem + u * p.A_stride + i);
+            rp_dispatch<P, Q, R>(acc, a, p.B + d.b_elem + i, p.B_stride, lane, d.shift);
         }
 #pragma unroll
-        for (int s = 0; s < W; ++s)
-            __stcs((float4*)(p.C + bk.c_elem + s * p.C_stride + i),
-                   make_float4(acc[s][0], acc[s][1], acc[s][2], acc[s][3]));
+        for (int s = 0; s < W; ++s) vstore_cs<R>(p.C + bk.c_elem + s * p.C_stride + i, acc[s]);
     }
 }
 
@@ -154,6 +260,12 @@ static bool runs_of(const int* off, int n, int& len, std::vector<int>& starts)
 
 static bool instantiated(int P, int Q) { return P == Q && P >= 2 && P <= 5; }
 
+static long long rp_rows_of(int P)
+{
+    return P == 2 ? rp_tile_rows<2>() : P == 3 ? rp_tile_rows<3>()
+         : P == 4 ? rp_tile_rows<4>() : rp_tile_rows<5>();
+}
+
 /* Builds the run-pair plan; returns false (and leaves *rp empty) when the
  * offsets do not have the structure or the interior is too small. */
 bool runpair_plan_build(const int* hA, int nA, const int* hB, int nB, const int* hC, int nC,
@@ -181,15 +293,19 @@ bool runpair_plan_build(const int* hA, int nA, const int* hB, int nB, const int*
         if (cidx[(int)kv.first] + W - 1 != cidx[(int)(kv.first + W - 1)]) return false;
     }
     const int dmin = *std::min_element(hA, hA + nA), dmax = *std::max_element(hA, hA + nA);
-    long long lo = std::max<long long>(rows_lo, (long long)b_lo - dmin + 16);
-    long long hi = std::min<long long>(rows_hi, (long long)b_hi - dmax - 16);
+    const long long T = rp_rows_of(P), R = T / kRpThreads;
+    /* the chunks a thread loads reach at most R - 1 rows before its first
+     * B row and 3R past its last */
+    if (A_stride % R || B_stride % R || C_stride % R) return false;
+    long long lo = std::max<long long>(rows_lo, (long long)b_lo - dmin + 4 * R);
+    long long hi = std::min<long long>(rows_hi, (long long)b_hi - dmax - 4 * R);
     lo = std::max<long long>(lo, 0);
-    lo += ((vrow0 - lo) % 4 + 4) % 4;
-    if (hi - lo < 2LL * kRpRows) return false;
+    lo += ((vrow0 - lo) % R + R) % R;
+    if (hi - lo < 2LL * T) return false;
     rp->P = P;
     rp->Q = Q;
     rp->i_lo = (int)lo;
-    rp->i_hi = (int)(lo + (hi - lo) / kRpRows * kRpRows);
+    rp->i_hi = (int)(lo + (hi - lo) / T * T);
     std::vector<RunBlock> bl;
     std::vector<RunPairDesc> ds;
     for (auto& kv : blocks) {
@@ -204,7 +320,7 @@ bool runpair_plan_build(const int* hA, int nA, const int* hB, int nB, const int*
         for (auto& pr : pairs) {
             const long long alpha = hA[pr.first];
             RunPairDesc d;
-            d.shift = (int)(((lo + alpha - b_vrow0) % 4 + 4) % 4);
+            d.shift = (int)(((lo + alpha - b_vrow0) % R + R) % R);
             d.a_elem = (long long)pr.first * A_stride - vrow0;
             d.b_elem = (long long)pr.second * B_stride - b_vrow0 + alpha - d.shift;
             d.pad = 0;
@@ -250,7 +366,7 @@ int runpair_launch(const RunPairPlan* rp, const float* A, const float* B, float*
     a.C_stride = C_stride;
     a.nblk = rp->nblk;
     a.i_lo = (int)tlo;
-    a.ntiles = (int)((thi - tlo) / kRpRows);
+    a.ntiles = (int)((thi - tlo) / rp_rows_of(rp->P));
     if (a.ntiles <= 0) return DIA_OK;
     const void* k = rp->P == 2 ? (const void*)runpair_kernel<2, 2>
                   : rp->P == 3 ? (const void*)runpair_kernel<3, 3>
@@ -263,6 +379,13 @@ int runpair_launch(const RunPairPlan* rp, const float* A, const float* B, float*
     return DIA_OK;
 }
 
-int runpair_tile_rows() { return kRpRows; }
+int runpair_tile_rows(const RunPairPlan* rp) { return (int)rp_rows_of(rp->P); }
+
+/* The kernel's vector loads and stores need buffers aligned to R floats. */
+bool runpair_aligned(const RunPairPlan* rp, const void* A, const void* B, const void* C)
+{
+    const uintptr_t m = (uintptr_t)(4 * (rp_rows_of(rp->P) / kRpThreads)) - 1;
+    return (((uintptr_t)A | (uintptr_t)B | (uintptr_t)C) & m) == 0;
+}
 
 }  // namespace dia

@@ -46,7 +46,8 @@ void runpair_plan_free(RunPairPlan* rp);
 int runpair_launch(const RunPairPlan* rp, const float* A, const float* B, float* C,
                    long long A_stride, long long B_stride, long long C_stride, long long tlo,
                    long long thi, cudaStream_t stream);
-int runpair_tile_rows();
+int runpair_tile_rows(const RunPairPlan* rp);
+bool runpair_aligned(const RunPairPlan* rp, const void* A, const void* B, const void* C);
 
 
 constexpr int kClusterSpan = 64;       /* max span of one A-offset cluster */
@@ -372,7 +373,7 @@ extern "C" int dia_spmspm_plan_info(const DiaSpmspmPlan* P, int* n_c, int* h_C_o
         if (h_C_start) h_C_start[c] = P->C_start[c];
     }
     if (P->rp.P) {
-        if (tile_rows) *tile_rows = -runpair_tile_rows();   /* negative: run-pair kernel */
+        if (tile_rows) *tile_rows = -runpair_tile_rows(&P->rp);   /* negative: run-pair kernel */
         if (tiled_lo) *tiled_lo = P->rp.i_lo;
         if (tiled_hi) *tiled_hi = P->rp.i_hi;
         return DIA_OK;
@@ -395,8 +396,8 @@ extern "C" int dia_spmspm_plan_execute(const DiaSpmspmPlan* P, const float* d_A_
         return fail(DIA_ERR_INVALID, "dia_spmspm_plan_execute: null pointer");
     long long tlo = row_hi, thi = row_hi;
     int kind = 0;   /* interior kernel: 1 run-pair, 2 tiled */
-    if (use_tiles && P->rp.P) {
-        const long long T = runpair_tile_rows();
+    if (use_tiles && P->rp.P && runpair_aligned(&P->rp, d_A_vals, d_B_vals, d_C_vals)) {
+        const long long T = runpair_tile_rows(&P->rp);
         const long long first = std::max<long long>(0, (row_lo - P->rp.i_lo + T - 1) / T);
         const long long last = (std::min<long long>(row_hi, P->rp.i_hi) - P->rp.i_lo) / T;
         if (last > first && row_lo < P->rp.i_hi) {

@@ -174,7 +174,21 @@ def _window_oracle(n, offs, W, wlo, lo, hi, C_off):
     return out
 
 
-@pytest.mark.parametrize("case", ["stencil7", "stencil27", "runs2", "band", "scatter", "tiny"])
+def _runs(starts, P):
+    return np.array([s + u for s in starts for u in range(P)], np.int32)
+
+
+# runs of 3, 4 and 5 whose starts fall on different residues mod 8, so the
+# run-pair kernel meets many alignment shifts of its B windows
+RUN_CASES = {
+    "runs3": (150_001, _runs([-2824, -2181, 409, 1558, 2261], 3)),
+    "runs4": (120_003, _runs([-1478, -572, 2155, 2928], 4)),
+    "runs5": (90_001, _runs([457, 1102, 1159, 2491], 5)),
+}
+
+
+@pytest.mark.parametrize("case", ["stencil7", "stencil27", "runs2", "band", "scatter", "tiny",
+                                  *RUN_CASES])
 def test_tiled_plan_equals_generic(case):
     """The shared-memory-tiled path, the planned generic path and the
     unplanned entry point give identical results (and the tiled kernel is
@@ -191,15 +205,18 @@ def test_tiled_plan_equals_generic(case):
         n, offs = 100_003, np.arange(-9, 10, dtype=np.int32)
     elif case == "scatter":
         n, offs = 300_000, _scatter_offsets(5)
+    elif case in RUN_CASES:
+        n, offs = RUN_CASES[case]
     else:
         n, offs = 300, np.array([-2, 0, 1], np.int32)
     A = dg.DiaRows.synth(n, n, offs, seed=71)
-    boffs = offs if case in ("stencil27", "runs2") else offs[::-1].copy()
+    runs = case in ("stencil27", "runs2", *RUN_CASES)
+    boffs = offs if runs else offs[::-1].copy()
     B = dg.DiaRows.synth(n, n, boffs, seed=72)
     plan = dg.SpmspmPlan(A, B)
     if case in ("stencil7", "band", "scatter"):   # shared-memory-tiled kernel
         assert plan.tile_rows > 0 and plan.tiled[1] > plan.tiled[0]
-    if case in ("stencil27", "runs2"):     # register-blocked run-pair kernel
+    if runs:     # register-blocked run-pair kernel
         assert plan.tile_rows < 0 and plan.tiled[1] > plan.tiled[0]
     Ct = plan.execute(A, B, plan.new_C())
     Cg = plan.execute(A, B, plan.new_C(), use_tiles=False)
@@ -212,3 +229,25 @@ def test_tiled_plan_equals_generic(case):
     for lo, hi in ((0, 1000), (1000, n // 2 + 7), (n // 2 + 7, n)):
         plan.execute(A, B, Cs, lo, hi)
     assert same(Cs.vals.cpu().numpy(), hu)
+
+
+@pytest.mark.parametrize("case", list(RUN_CASES))
+def test_runpair_b_window_shifts(case):
+    """Row-window products whose B block starts at every residue mod 8 (as
+    a partitioned product's halo does) match the whole product's rows bit
+    for bit, with the run-pair kernel doing the interior."""
+    n, offs = RUN_CASES[case]
+    A = dg.DiaRows.synth(n, n, offs, seed=81)
+    Cm = dg.spmspm(A, A)
+    H = int(np.abs(offs).max())
+    Ah = A.vals.cpu().numpy()
+    for delta in range(8):
+        lo, hi = n // 3 + delta, n // 3 + delta + 20_000
+        wlo, whi = lo - H - delta, hi + H + 3
+        Aw = dg.DiaRows.from_host(n, n, offs, Ah[:, wlo:whi], vrow0=wlo)
+        Aa = dg.DiaRows.from_host(n, n, offs, Ah[:, lo:hi], vrow0=lo)
+        plan = dg.SpmspmPlan(Aa, Aw)
+        assert plan.tile_rows < 0 and plan.tiled[1] > plan.tiled[0], delta
+        Cw = dg.DiaRows.empty(n, n, Cm.offsets, vrow0=lo, nrows=hi - lo)
+        dg.spmspm(Aa, Aw, Cw)
+        assert same(Cm.vals[:, lo:hi].cpu().numpy(), Cw.vals[:, :hi - lo].cpu().numpy()), delta
