@@ -134,10 +134,13 @@ __device__ __forceinline__ void rp_body(float (&acc)[P + Q - 1][R], const float 
     constexpr int L = P + R - 1;                 /* window length */
     constexpr int NQ = (D + L - 1) / R + 1;      /* chunks the window touches */
     constexpr int OWN = rp_own(D, L, R);
-    float w[Q][L];
+    /* v descends outermost and u ascends inside it, so every output
+     * (u + v fixed) still takes its terms in ascending u; only one B
+     * window is live at a time */
 #pragma unroll
-    for (int v = 0; v < Q; ++v) {
+    for (int v = Q - 1; v >= 0; --v) {
         const float* cp = bp + v * B_stride;
+        float w[L];
         float own[R];
         vload<R>(own, cp + OWN * R);
 #pragma unroll
@@ -145,7 +148,7 @@ __device__ __forceinline__ void rp_body(float (&acc)[P + Q - 1][R], const float 
             if (q == OWN) {
 #pragma unroll
                 for (int p = D; p < D + L; ++p)
-                    if (p / R == q) w[v][p - D] = own[p % R];
+                    if (p / R == q) w[p - D] = own[p % R];
                 continue;
             }
             /* lanes whose neighbour lane + (q - OWN) lies outside the warp
@@ -160,17 +163,15 @@ __device__ __forceinline__ void rp_body(float (&acc)[P + Q - 1][R], const float 
             for (int p = D; p < D + L; ++p)
                 if (p / R == q) {
                     const float sh = __shfl_sync(0xffffffffu, own[p % R], src & 31);
-                    w[v][p - D] = outside ? fx[p % R] : sh;
+                    w[p - D] = outside ? fx[p % R] : sh;
                 }
         }
-    }
 #pragma unroll
-    for (int u = 0; u < P; ++u)
-#pragma unroll
-        for (int v = 0; v < Q; ++v)
+        for (int u = 0; u < P; ++u)
 #pragma unroll
             for (int j = 0; j < R; ++j)
-                acc[u + v][j] = mul_add_rn(acc[u + v][j], a[u][j], w[v][u + j]);
+                acc[u + v][j] = mul_add_rn(acc[u + v][j], a[u][j], w[u + j]);
+    }
 }
 
 template <int P, int Q, int R>
