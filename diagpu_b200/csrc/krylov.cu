@@ -81,6 +81,21 @@ lanczos_spmv_kernel(KrArgs a, const float* __restrict__ v, const float* __restri
     if (threadIdx.x == 0) part[blockIdx.x] = t;
 }
 
+/* sum of part[0..nb) in the reduce kernel's fixed order, in every thread
+ * of the CTA: each CTA of a consumer kernel repeats it and gets the same
+ * bits, which saves the single-CTA reduce launch between two vector
+ * kernels (nb doubles, a few KB, come from L2) */
+__device__ __forceinline__ double all_sum(const double* __restrict__ part, int nb)
+{
+    __shared__ double s_t;
+    double acc = 0.0;
+    for (int b = threadIdx.x; b < nb; b += kKrThreads) acc += part[b];
+    const double t = block_sum(acc);
+    if (threadIdx.x == 0) s_t = t;
+    __syncthreads();
+    return s_t;
+}
+
 /* one CTA: out = sum of part[0..nb) in a fixed order, sqrt when asked */
 __global__ void __launch_bounds__(kKrThreads)
 lanczos_reduce_kernel(const double* __restrict__ part, int nb, double* __restrict__ out, int root)
@@ -91,12 +106,16 @@ lanczos_reduce_kernel(const double* __restrict__ part, int nb, double* __restric
     if (threadIdx.x == 0) *out = root ? sqrt(t) : t;
 }
 
-/* w = w - fl(alpha * v); part[b] = sum of w^2 */
+/* alpha = sum of the SpMV's partials (CTA 0 records it); w = w -
+ * fl(alpha * v); part_out[b] = sum of w^2 */
 __global__ void __launch_bounds__(kKrThreads)
-lanczos_orth_kernel(int n, const float* __restrict__ v, const double* __restrict__ alpha,
-                    float* __restrict__ w, double* __restrict__ part)
+lanczos_orth_kernel(int n, const float* __restrict__ v, const double* __restrict__ part_in,
+                    int nb, double* __restrict__ alpha, float* __restrict__ w,
+                    double* __restrict__ part_out)
 {
-    const float al = (float)*alpha;
+    const double ad = all_sum(part_in, nb);
+    if (blockIdx.x == 0 && threadIdx.x == 0) *alpha = ad;
+    const float al = (float)ad;
     double ss = 0.0;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -107,7 +126,7 @@ lanczos_orth_kernel(int n, const float* __restrict__ v, const double* __restrict
         ss += (double)wi * (double)wi;
     }
     const double t = block_sum(ss);
-    if (threadIdx.x == 0) part[blockIdx.x] = t;
+    if (threadIdx.x == 0) part_out[blockIdx.x] = t;
 }
 
 /* part[b] = sum of x^2 over the CTA's rows (x is only read) */
@@ -124,12 +143,15 @@ lanczos_norm_kernel(int n, const float* __restrict__ x, double* __restrict__ par
     if (threadIdx.x == 0) part[blockIdx.x] = t;
 }
 
-/* v_next = fl(w * fl(1 / norm)) */
+/* norm = sqrt(sum of the partials) (CTA 0 records it);
+ * v_next = fl(w * fl(1 / norm)) */
 __global__ void __launch_bounds__(kKrThreads)
-lanczos_scale_kernel(int n, const float* __restrict__ w, const double* __restrict__ norm,
-                     float* __restrict__ v_next)
+lanczos_scale_kernel(int n, const float* __restrict__ w, const double* __restrict__ part_in,
+                     int nb, double* __restrict__ norm, float* __restrict__ v_next)
 {
-    const float inv = __frcp_rn((float)*norm);
+    const double nd = sqrt(all_sum(part_in, nb));
+    if (blockIdx.x == 0 && threadIdx.x == 0) *norm = nd;
+    const float inv = __frcp_rn((float)nd);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const int i = blockIdx.x * kKrRows + j * kKrThreads + threadIdx.x;
@@ -145,7 +167,7 @@ extern "C" int64_t dia_lanczos_workspace(int64_t n)
 {
     if (n <= 0) return -1;
     const int64_t nb = (n + kKrRows - 1) / kKrRows;
-    return 4 * n * 4 + nb * 8 + 64;
+    return 4 * n * 4 + 2 * nb * 8 + 64;
 }
 
 extern "C" int dia_lanczos(int64_t n, int num_diags, const int* d_offsets, const float* d_vals,
@@ -166,16 +188,19 @@ extern "C" int dia_lanczos(int64_t n, int num_diags, const int* d_offsets, const
     const int nb = (int)((n + kKrRows - 1) / kKrRows);
     float* w = (float*)d_work;
     float* vbuf[3] = {w + n, w + 2 * n, w + 3 * n};
+    /* two partial-sum buffers: a kernel that reduces one writes the other */
     double* part = (double*)(((uintptr_t)(w + 4 * n) + 7) & ~(uintptr_t)7);
+    double* part2 = part + nb;
     double* norm0 = d_beta;   /* scratch for ||x|| before beta_0 is written */
     /* v_0 = x * fl(1/||x||) */
     lanczos_norm_kernel<<<nb, kKrThreads, 0, stream>>>((int)n, d_x, part);
     DIA_TRY_CUDA(cudaGetLastError());
-    lanczos_reduce_kernel<<<1, kKrThreads, 0, stream>>>(part, nb, norm0, 1);
-    DIA_TRY_CUDA(cudaGetLastError());
-    lanczos_scale_kernel<<<nb, kKrThreads, 0, stream>>>((int)n, d_x, norm0, vbuf[0]);
+    lanczos_scale_kernel<<<nb, kKrThreads, 0, stream>>>((int)n, d_x, part, nb, norm0, vbuf[0]);
     DIA_TRY_CUDA(cudaGetLastError());
     KrArgs a{d_vals, d_offsets, num_diags, (int)n, stride};
+    /* three launches per step: SpMV (+ alpha partials), orthogonalise
+     * (alpha reduced in every CTA, + beta partials), scale (beta reduced
+     * in every CTA); the last step reduces beta in one CTA */
     for (int j = 0; j < m; ++j) {
         float* v = vbuf[j % 3];
         float* vp = vbuf[(j + 2) % 3];
@@ -186,16 +211,15 @@ extern "C" int dia_lanczos(int64_t n, int num_diags, const int* d_offsets, const
         lanczos_spmv_kernel<<<nb, kKrThreads, 0, stream>>>(a, v, j ? vp : nullptr,
                                                           j ? d_beta + j - 1 : nullptr, w, part);
         DIA_TRY_CUDA(cudaGetLastError());
-        lanczos_reduce_kernel<<<1, kKrThreads, 0, stream>>>(part, nb, d_alpha + j, 0);
+        lanczos_orth_kernel<<<nb, kKrThreads, 0, stream>>>((int)n, v, part, nb, d_alpha + j, w,
+                                                          part2);
         DIA_TRY_CUDA(cudaGetLastError());
-        lanczos_orth_kernel<<<nb, kKrThreads, 0, stream>>>((int)n, v, d_alpha + j, w, part);
+        if (j + 1 < m)
+            lanczos_scale_kernel<<<nb, kKrThreads, 0, stream>>>((int)n, w, part2, nb, d_beta + j,
+                                                               vn);
+        else
+            lanczos_reduce_kernel<<<1, kKrThreads, 0, stream>>>(part2, nb, d_beta + j, 1);
         DIA_TRY_CUDA(cudaGetLastError());
-        lanczos_reduce_kernel<<<1, kKrThreads, 0, stream>>>(part, nb, d_beta + j, 1);
-        DIA_TRY_CUDA(cudaGetLastError());
-        if (j + 1 < m) {
-            lanczos_scale_kernel<<<nb, kKrThreads, 0, stream>>>((int)n, w, d_beta + j, vn);
-            DIA_TRY_CUDA(cudaGetLastError());
-        }
     }
     return DIA_OK;
 }
