@@ -362,7 +362,7 @@ def single_gpu_extras(dg, steps, warmup, hbm, src):
                             "(fused SpMV+dot, fp64 fixed-order reductions, no host sync)",
                 "metric": "lanczos_GBps", "value": round(byts / ms / 1e6, 1), "unit": "GB/s",
                 "ms": round(ms, 4), "bytes": byts, "roofline": roofline(byts / ms / 1e6, hbm, src),
-                "gpu_launches_per_step": 2 + 3 * LANCZOS_M})
+                "gpu_launches_per_step": 2 + 2 * LANCZOS_M})
     # complex64 SpMV (Hamiltonian-type operators), 27-point stencil on 256^3
     fn, byts = _only_spmv_c64(dg)
     ms = timed(fn, max(3, steps // 5), min(warmup, 3))

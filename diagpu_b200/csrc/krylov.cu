@@ -51,36 +51,6 @@ struct KrArgs {
     long long stride;
 };
 
-/* w = fl(A v) - fl(beta_prev * v_prev); part[b] = sum over the CTA's rows of w*v */
-__global__ void __launch_bounds__(kKrThreads)
-lanczos_spmv_kernel(KrArgs a, const float* __restrict__ v, const float* __restrict__ v_prev,
-                    const double* __restrict__ beta_prev, float* __restrict__ w,
-                    double* __restrict__ part)
-{
-    __shared__ int s_off[kMaxTerms];
-    const int K = min(a.K, kMaxTerms);
-    for (int k = threadIdx.x; k < K; k += kKrThreads) s_off[k] = a.off[k];
-    __syncthreads();
-    const float bp = beta_prev ? (float)*beta_prev : 0.0f;
-    double dot = 0.0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int i = blockIdx.x * kKrRows + j * kKrThreads + threadIdx.x;
-        if (i >= a.n) continue;
-        float s = 0.0f;
-        for (int k = 0; k < K; ++k) {
-            const int c = i + s_off[k];
-            if (c < 0 || c >= a.n) continue;
-            s = __fadd_rn(s, __fmul_rn(__ldcs(a.vals + (long long)k * a.stride + i), __ldg(v + c)));
-        }
-        const float wi = beta_prev ? __fsub_rn(s, __fmul_rn(bp, v_prev[i])) : s;
-        w[i] = wi;
-        dot += (double)wi * (double)v[i];
-    }
-    const double t = block_sum(dot);
-    if (threadIdx.x == 0) part[blockIdx.x] = t;
-}
-
 /* sum of part[0..nb) in the reduce kernel's fixed order, in every thread
  * of the CTA: each CTA of a consumer kernel repeats it and gets the same
  * bits, which saves the single-CTA reduce launch between two vector
@@ -94,6 +64,48 @@ __device__ __forceinline__ double all_sum(const double* __restrict__ part, int n
     if (threadIdx.x == 0) s_t = t;
     __syncthreads();
     return s_t;
+}
+
+/* One Lanczos step's SpMV with the previous step's scaling fused in:
+ *     beta = sqrt(sum of part_in)  (every CTA, fixed order; CTA 0 records it
+ *            in beta_rec unless null),  inv = fl(1 / beta),
+ *     v[c] = fl(wsrc[c] * inv)     (computed wherever the SpMV reads it; the
+ *            CTA's own rows are stored in v_out),
+ *     w    = fl(A v) - fl(beta * v_prev)   (no v_prev in the first step),
+ *     part_out[b] = sum over the CTA's rows of w * v.
+ * The first step scales x by its norm the same way. */
+__global__ void __launch_bounds__(kKrThreads)
+lanczos_spmv_kernel(KrArgs a, const float* __restrict__ wsrc, const double* __restrict__ part_in,
+                    int nb, double* __restrict__ beta_rec, const float* __restrict__ v_prev,
+                    float* __restrict__ v_out, float* __restrict__ w, double* __restrict__ part)
+{
+    __shared__ int s_off[kMaxTerms];
+    const int K = min(a.K, kMaxTerms);
+    for (int k = threadIdx.x; k < K; k += kKrThreads) s_off[k] = a.off[k];
+    const double bd = sqrt(all_sum(part_in, nb));   /* synchronises s_off too */
+    if (beta_rec && blockIdx.x == 0 && threadIdx.x == 0) *beta_rec = bd;
+    const float inv = __frcp_rn((float)bd);
+    const float bp = (float)bd;
+    double dot = 0.0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int i = blockIdx.x * kKrRows + j * kKrThreads + threadIdx.x;
+        if (i >= a.n) continue;
+        float s = 0.0f;
+        for (int k = 0; k < K; ++k) {
+            const int c = i + s_off[k];
+            if (c < 0 || c >= a.n) continue;
+            s = __fadd_rn(s, __fmul_rn(__ldcs(a.vals + (long long)k * a.stride + i),
+                                       __fmul_rn(__ldg(wsrc + c), inv)));
+        }
+        const float vi = __fmul_rn(wsrc[i], inv);
+        v_out[i] = vi;
+        const float wi = v_prev ? __fsub_rn(s, __fmul_rn(bp, v_prev[i])) : s;
+        w[i] = wi;
+        dot += (double)wi * (double)vi;
+    }
+    const double t = block_sum(dot);
+    if (threadIdx.x == 0) part[blockIdx.x] = t;
 }
 
 /* one CTA: out = sum of part[0..nb) in a fixed order, sqrt when asked */
@@ -143,22 +155,6 @@ lanczos_norm_kernel(int n, const float* __restrict__ x, double* __restrict__ par
     if (threadIdx.x == 0) part[blockIdx.x] = t;
 }
 
-/* norm = sqrt(sum of the partials) (CTA 0 records it);
- * v_next = fl(w * fl(1 / norm)) */
-__global__ void __launch_bounds__(kKrThreads)
-lanczos_scale_kernel(int n, const float* __restrict__ w, const double* __restrict__ part_in,
-                     int nb, double* __restrict__ norm, float* __restrict__ v_next)
-{
-    const double nd = sqrt(all_sum(part_in, nb));
-    if (blockIdx.x == 0 && threadIdx.x == 0) *norm = nd;
-    const float inv = __frcp_rn((float)nd);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int i = blockIdx.x * kKrRows + j * kKrThreads + threadIdx.x;
-        if (i < n) v_next[i] = __fmul_rn(w[i], inv);
-    }
-}
-
 }  // namespace dia
 
 using namespace dia;
@@ -187,38 +183,38 @@ extern "C" int dia_lanczos(int64_t n, int num_diags, const int* d_offsets, const
         return fail(DIA_ERR_INVALID, "dia_lanczos: workspace smaller than dia_lanczos_workspace()");
     const int nb = (int)((n + kKrRows - 1) / kKrRows);
     float* w = (float*)d_work;
-    float* vbuf[3] = {w + n, w + 2 * n, w + 3 * n};
+    float* wbuf[2] = {w, w + n};
+    float* vbuf[2] = {w + 2 * n, w + 3 * n};
     /* two partial-sum buffers: a kernel that reduces one writes the other */
     double* part = (double*)(((uintptr_t)(w + 4 * n) + 7) & ~(uintptr_t)7);
     double* part2 = part + nb;
-    double* norm0 = d_beta;   /* scratch for ||x|| before beta_0 is written */
-    /* v_0 = x * fl(1/||x||) */
-    lanczos_norm_kernel<<<nb, kKrThreads, 0, stream>>>((int)n, d_x, part);
-    DIA_TRY_CUDA(cudaGetLastError());
-    lanczos_scale_kernel<<<nb, kKrThreads, 0, stream>>>((int)n, d_x, part, nb, norm0, vbuf[0]);
-    DIA_TRY_CUDA(cudaGetLastError());
     KrArgs a{d_vals, d_offsets, num_diags, (int)n, stride};
-    /* three launches per step: SpMV (+ alpha partials), orthogonalise
-     * (alpha reduced in every CTA, + beta partials), scale (beta reduced
-     * in every CTA); the last step reduces beta in one CTA */
+    /* ||x||^2 partials; the first SpMV scales x by the norm */
+    lanczos_norm_kernel<<<nb, kKrThreads, 0, stream>>>((int)n, d_x, part2);
+    DIA_TRY_CUDA(cudaGetLastError());
+    /* two launches per step: SpMV (the previous step's scaling fused in,
+     * + alpha partials) and orthogonalise (alpha reduced in every CTA,
+     * + beta partials); the last beta is reduced in one CTA.  The SpMV reads
+     * the previous w while writing the new one, so w alternates between two
+     * buffers (and v with it) */
     for (int j = 0; j < m; ++j) {
-        float* v = vbuf[j % 3];
-        float* vp = vbuf[(j + 2) % 3];
-        float* vn = vbuf[(j + 1) % 3];
+        float* v = vbuf[j & 1];
+        float* vp = vbuf[(j + 1) & 1];
+        float* wj = wbuf[j & 1];
+        const float* wsrc = j ? wbuf[(j + 1) & 1] : d_x;
+        lanczos_spmv_kernel<<<nb, kKrThreads, 0, stream>>>(a, wsrc, part2, nb,
+                                                          j ? d_beta + j - 1 : nullptr,
+                                                          j ? vp : nullptr, v, wj, part);
+        DIA_TRY_CUDA(cudaGetLastError());
         if (d_basis)
             DIA_TRY_CUDA(cudaMemcpyAsync(d_basis + (size_t)j * n, v, (size_t)n * 4,
                                          cudaMemcpyDeviceToDevice, stream));
-        lanczos_spmv_kernel<<<nb, kKrThreads, 0, stream>>>(a, v, j ? vp : nullptr,
-                                                          j ? d_beta + j - 1 : nullptr, w, part);
-        DIA_TRY_CUDA(cudaGetLastError());
-        lanczos_orth_kernel<<<nb, kKrThreads, 0, stream>>>((int)n, v, part, nb, d_alpha + j, w,
+        lanczos_orth_kernel<<<nb, kKrThreads, 0, stream>>>((int)n, v, part, nb, d_alpha + j, wj,
                                                           part2);
         DIA_TRY_CUDA(cudaGetLastError());
-        if (j + 1 < m)
-            lanczos_scale_kernel<<<nb, kKrThreads, 0, stream>>>((int)n, w, part2, nb, d_beta + j,
-                                                               vn);
-        else
-            lanczos_reduce_kernel<<<1, kKrThreads, 0, stream>>>(part2, nb, d_beta + j, 1);
+    }
+    if (m > 0) {
+        lanczos_reduce_kernel<<<1, kKrThreads, 0, stream>>>(part2, nb, d_beta + m - 1, 1);
         DIA_TRY_CUDA(cudaGetLastError());
     }
     return DIA_OK;
