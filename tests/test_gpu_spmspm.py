@@ -251,3 +251,27 @@ def test_runpair_b_window_shifts(case):
         Cw = dg.DiaRows.empty(n, n, Cm.offsets, vrow0=lo, nrows=hi - lo)
         dg.spmspm(Aa, Aw, Cw)
         assert same(Cm.vals[:, lo:hi].cpu().numpy(), Cw.vals[:, :hi - lo].cpu().numpy()), delta
+
+
+def test_runpair_misaligned_buffers_fall_back():
+    """A C buffer that is not 32-byte aligned cannot take the run-pair
+    kernel's vector stores; the plan must then run the generic kernel and
+    still give the same values."""
+    import ctypes
+    n = 64 * 64 * 64
+    offs = np.array([i + 64 * j + 4096 * k for k in (-1, 0, 1) for j in (-1, 0, 1)
+                     for i in (-1, 0, 1)], np.int32)
+    A = dg.DiaRows.synth(n, n, offs, seed=91)
+    plan = dg.SpmspmPlan(A, A)
+    assert plan.tile_rows < 0
+    ref = plan.execute(A, A, plan.new_C())
+    Cr = ref.vals
+    flat = torch.zeros(Cr.numel() + 8, dtype=torch.float32, device="cuda")
+    rc = dg.lib().dia_spmspm_plan_execute(plan._h, ctypes.c_void_p(A.vals.data_ptr()),
+                                          ctypes.c_void_p(A.vals.data_ptr()),
+                                          ctypes.c_void_p(flat.data_ptr() + 4), 0, n, 1,
+                                          dg._stream())
+    assert rc == 0
+    torch.cuda.synchronize()
+    got = flat[1:1 + Cr.numel()].view_as(Cr)
+    assert same(Cr[:, :n].cpu().numpy(), got[:, :n].cpu().numpy())
