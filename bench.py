@@ -643,7 +643,15 @@ def run_ours(args):
     if world == 1:
         extras = single_gpu_extras(dg, K, W, hbm, src)
         if not args.no_cpu_baseline:
-            cpu = cpu_port_baseline()
+            ref = reference_cpu_spmv(5, 1)
+            if ref is None:
+                cpu = cpu_port_baseline()
+            else:
+                _, v_ref, thr_ref, S_ref = ref
+                cpu = {"value": v_ref, "unit": "GB/s", "cores": thr_ref, "kind": "reference",
+                       "sample": f"spmv_from_recon (spmv/test/test_tc_spmv.cu:64-79) on rows "
+                                 f"[0, {S_ref}) of config 5 (1/16 of it), mean of 5, "
+                                 f"{thr_ref} threads over row slices; a rate on the sample"}
     clocks = None
     if clk is not None:
         clk.__exit__(None, None, None)
@@ -824,19 +832,18 @@ def reference_gpu_leg(steps, warmup):
     return out
 
 
-def run_reference(args):
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
-        return
+def reference_cpu_spmv(steps, warmup):
+    """The reference's own CPU SpMV, spmv_from_recon
+    (spmv/test/test_tc_spmv.cu:64-79, compiled from the reference sources
+    into oracle/_ref/), over rows [0, REF_SAMPLE_ROWS) of config 5 in the
+    Recon layout, threaded over row slices.  Returns (ms per call, GB/s,
+    threads, rows) or None when the library was not built."""
     import ctypes as C
 
     import oracle
     lib = oracle.ref("spmv")
     if lib is None:
-        print(json.dumps({"impl": "reference", "unavailable":
-                          "oracle/_ref/libref_spmv.so not built (needs the reference sources)"}))
-        return
+        return None
     S = REF_SAMPLE_ROWS
     dmax = int(OFF5.max())
     rows = oracle.synth_rowidx(SEED_A, N5, N5, OFF5, row0=0, nrows=S)
@@ -859,11 +866,24 @@ def run_reference(args):
     p = lambda a: a.ctypes.data_as(C.c_void_p)
     call = lambda reps: lib.ref_spmv_from_recon_threads(S, cols, len(desc), p(desc), p(rec), p(x),
                                                         p(y), thr, reps)
-    if args.warmup:
-        call(args.warmup)
-    ms = call(args.steps)
+    if warmup:
+        call(warmup)
+    ms = call(steps)
     b, _ = spmv_bytes(N5, OFF5, 0, S)
-    v = round(b / ms / 1e6, 2)
+    return ms, round(b / ms / 1e6, 2), thr, S
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    ref = reference_cpu_spmv(args.steps, args.warmup)
+    if ref is None:
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "oracle/_ref/libref_spmv.so not built (needs the reference sources)"}))
+        return
+    ms, v, thr, S = ref
     if world == 1 and torch.cuda.is_available() and not args.no_ref_gpu:
         for entry in reference_gpu_leg(args.steps, args.warmup):
             emit({"reference_gpu": entry})
