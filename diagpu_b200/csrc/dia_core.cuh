@@ -61,7 +61,7 @@ __device__ __forceinline__ float mul_add_rn(float acc, float a, float b)
  * so one memory latency is paid per batch instead of per term; the adds are
  * still applied term by term in list order.  Terms that cover the tile only
  * partly take the per-row checked path; others are skipped. */
-template <bool STREAM_U, int ILP = kILP, int BATCH = kBatch, bool PARTIAL = false>
+template <bool STREAM_U, int ILP = kILP, int BATCH = kBatch>
 __device__ __forceinline__ void accumulate_terms(const float* __restrict__ U,
                                                  const float* __restrict__ V,
                                                  const Term* s_terms, int nt,
@@ -73,22 +73,18 @@ __device__ __forceinline__ void accumulate_terms(const float* __restrict__ U,
     constexpr int kBatch = BATCH;
     const int tile_hi = tile_lo + kTile;
     int q = 0;
-    for (; PARTIAL ? q < nt : q + kBatch <= nt; q += kBatch) {
-        const int nb = PARTIAL ? min(kBatch, nt - q) : kBatch;
+    for (; q + kBatch <= nt; q += kBatch) {
         Term t[kBatch];
         bool full = true;
 #pragma unroll
         for (int u = 0; u < kBatch; ++u) {
-            if (u < nb) {
-                t[u] = s_terms[q + u];
-                full &= (t[u].lo <= tile_lo) & (tile_hi <= t[u].hi);
-            }
+            t[u] = s_terms[q + u];
+            full &= (t[u].lo <= tile_lo) & (tile_hi <= t[u].hi);
         }
         if (!full) break;
         float a[kBatch][kILP], b[kBatch][kILP];
 #pragma unroll
         for (int u = 0; u < kBatch; ++u) {
-            if (u >= nb) continue;
             const float* __restrict__ up = U + t[u].u + r0;
             const float* __restrict__ vp = V + t[u].v + r0;
 #pragma unroll
@@ -99,9 +95,8 @@ __device__ __forceinline__ void accumulate_terms(const float* __restrict__ U,
         }
 #pragma unroll
         for (int u = 0; u < kBatch; ++u)
-            if (u < nb)
 #pragma unroll
-                for (int j = 0; j < kILP; ++j) acc[j] = mul_add_rn(acc[j], a[u][j], b[u][j]);
+            for (int j = 0; j < kILP; ++j) acc[j] = mul_add_rn(acc[j], a[u][j], b[u][j]);
     }
     for (; q < nt; ++q) {
         const Term t = s_terms[q];

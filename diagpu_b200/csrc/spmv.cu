@@ -20,8 +20,6 @@
 #include "../../include/diagpu_b200.h"
 #include "dia_core.cuh"
 
-#include <cstdlib>
-
 namespace dia {
 
 struct SpmvArgs {
@@ -41,11 +39,9 @@ struct SpmvArgs {
     float* sum;
 };
 
-template <bool STREAM, bool EPI = false, int ILP = kILP, int BATCH = kBatch, bool PARTIAL = false>
+template <bool STREAM, bool EPI = false>
 __global__ void __launch_bounds__(kBlock) spmv_kernel(SpmvArgs a)
 {
-    constexpr int kILP = ILP;
-    constexpr int kTile = kBlock * ILP;
     __shared__ Term s_t[kMaxTerms];
     const int tile_lo = a.row_lo + (int)blockIdx.x * kTile;
     const int r0 = tile_lo + (int)threadIdx.x;
@@ -73,7 +69,7 @@ __global__ void __launch_bounds__(kBlock) spmv_kernel(SpmvArgs a)
             s_t[q] = t;
         }
         __syncthreads();
-        accumulate_terms<STREAM, ILP, BATCH, PARTIAL>(a.vals, a.x, s_t, nt, tile_lo, r0, acc);
+        accumulate_terms<STREAM>(a.vals, a.x, s_t, nt, tile_lo, r0, acc);
     }
 #pragma unroll
     for (int j = 0; j < kILP; ++j) {
@@ -94,24 +90,6 @@ static int launch_spmv(const SpmvArgs& a, cudaStream_t stream)
 {
     const long long rows = (long long)a.row_hi - a.row_lo;
     if (rows <= 0) return DIA_OK;
-    static const int vm = [] { const char* e = getenv("DIA_SPMV_V"); return e ? atoi(e) : 0; }();
-    if (vm && a.K <= 8) {
-        if (vm == 1) {
-            const long long g = (rows + kBlock * 2 - 1) / (kBlock * 2);
-            if (a.sum) spmv_kernel<true, true, 2, 8, true><<<(unsigned)g, kBlock, 0, stream>>>(a);
-            else spmv_kernel<true, false, 2, 8, true><<<(unsigned)g, kBlock, 0, stream>>>(a);
-        } else if (vm == 2) {
-            const long long g = (rows + kBlock - 1) / kBlock;
-            if (a.sum) spmv_kernel<true, true, 1, 8, true><<<(unsigned)g, kBlock, 0, stream>>>(a);
-            else spmv_kernel<true, false, 1, 8, true><<<(unsigned)g, kBlock, 0, stream>>>(a);
-        } else {
-            const long long g = (rows + kTile - 1) / kTile;
-            if (a.sum) spmv_kernel<true, true, 4, 8, true><<<(unsigned)g, kBlock, 0, stream>>>(a);
-            else spmv_kernel<true, false, 4, 4, true><<<(unsigned)g, kBlock, 0, stream>>>(a);
-        }
-        DIA_TRY_CUDA(cudaGetLastError());
-        return DIA_OK;
-    }
     const long long grid = (rows + kTile - 1) / kTile;
     if (a.sum)
         spmv_kernel<true, true><<<(unsigned)grid, kBlock, 0, stream>>>(a);
