@@ -74,6 +74,7 @@ __device__ __forceinline__ double all_sum(const double* __restrict__ part, int n
  *     w    = fl(A v) - fl(beta * v_prev)   (no v_prev in the first step),
  *     part_out[b] = sum over the CTA's rows of w * v.
  * The first step scales x by its norm the same way. */
+template <bool CACHE>
 __global__ void __launch_bounds__(kKrThreads)
 lanczos_spmv_kernel(KrArgs a, const float* __restrict__ wsrc, const double* __restrict__ part_in,
                     int nb, double* __restrict__ beta_rec, const float* __restrict__ v_prev,
@@ -95,7 +96,8 @@ lanczos_spmv_kernel(KrArgs a, const float* __restrict__ wsrc, const double* __re
         for (int k = 0; k < K; ++k) {
             const int c = i + s_off[k];
             if (c < 0 || c >= a.n) continue;
-            s = __fadd_rn(s, __fmul_rn(__ldcs(a.vals + (long long)k * a.stride + i),
+            const float* vp = a.vals + (long long)k * a.stride + i;
+            s = __fadd_rn(s, __fmul_rn(CACHE ? __ldg(vp) : __ldcs(vp),
                                        __fmul_rn(__ldg(wsrc + c), inv)));
         }
         const float vi = __fmul_rn(wsrc[i], inv);
@@ -189,6 +191,10 @@ extern "C" int dia_lanczos(int64_t n, int num_diags, const int* d_offsets, const
     double* part = (double*)(((uintptr_t)(w + 4 * n) + 7) & ~(uintptr_t)7);
     double* part2 = part + nb;
     KrArgs a{d_vals, d_offsets, num_diags, (int)n, stride};
+    /* every step reads the whole matrix: when its values fit in about half
+     * of L2 they are read with normal caching and stay there across steps;
+     * larger operators stream (evict-first) */
+    const bool cache = (long long)num_diags * stride * 4 <= (48LL << 20);
     /* ||x||^2 partials; the first SpMV scales x by the norm */
     lanczos_norm_kernel<<<nb, kKrThreads, 0, stream>>>((int)n, d_x, part2);
     DIA_TRY_CUDA(cudaGetLastError());
@@ -202,9 +208,12 @@ extern "C" int dia_lanczos(int64_t n, int num_diags, const int* d_offsets, const
         float* vp = vbuf[(j + 1) & 1];
         float* wj = wbuf[j & 1];
         const float* wsrc = j ? wbuf[(j + 1) & 1] : d_x;
-        lanczos_spmv_kernel<<<nb, kKrThreads, 0, stream>>>(a, wsrc, part2, nb,
-                                                          j ? d_beta + j - 1 : nullptr,
-                                                          j ? vp : nullptr, v, wj, part);
+        if (cache)
+            lanczos_spmv_kernel<true><<<nb, kKrThreads, 0, stream>>>(
+                a, wsrc, part2, nb, j ? d_beta + j - 1 : nullptr, j ? vp : nullptr, v, wj, part);
+        else
+            lanczos_spmv_kernel<false><<<nb, kKrThreads, 0, stream>>>(
+                a, wsrc, part2, nb, j ? d_beta + j - 1 : nullptr, j ? vp : nullptr, v, wj, part);
         DIA_TRY_CUDA(cudaGetLastError());
         if (d_basis)
             DIA_TRY_CUDA(cudaMemcpyAsync(d_basis + (size_t)j * n, v, (size_t)n * 4,

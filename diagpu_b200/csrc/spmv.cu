@@ -22,6 +22,9 @@
 
 namespace dia {
 
+/* operator size below which chained products keep the values in L2 */
+constexpr long long kL2KeepBytes = 48LL << 20;
+
 struct SpmvArgs {
     const float* vals;
     const float* x;
@@ -37,6 +40,7 @@ struct SpmvArgs {
     long long y_base;     /* y element of row i is y[i - y_base] */
     float scale;          /* EPI: y = scale * (A x) and sum += y */
     float* sum;
+    int cache_vals;       /* 1: values read with normal caching (kept in L2 across launches) */
 };
 
 template <bool STREAM, bool EPI = false>
@@ -91,7 +95,9 @@ static int launch_spmv(const SpmvArgs& a, cudaStream_t stream)
     const long long rows = (long long)a.row_hi - a.row_lo;
     if (rows <= 0) return DIA_OK;
     const long long grid = (rows + kTile - 1) / kTile;
-    if (a.sum)
+    if (a.sum && a.cache_vals)
+        spmv_kernel<false, true><<<(unsigned)grid, kBlock, 0, stream>>>(a);
+    else if (a.sum)
         spmv_kernel<true, true><<<(unsigned)grid, kBlock, 0, stream>>>(a);
     else
         spmv_kernel<true><<<(unsigned)grid, kBlock, 0, stream>>>(a);
@@ -194,6 +200,10 @@ extern "C" int dia_expm_taylor(int64_t n, int num_diags, const int* d_offsets, c
     if (n + kTile >= (1LL << 31))
         return fail(DIA_ERR_UNSUPPORTED, "dia_expm_taylor: n beyond int32 range");
     DIA_TRY_CUDA(cudaMemcpyAsync(d_y, d_x, (size_t)n * 4, cudaMemcpyDeviceToDevice, stream));
+    /* every term reads the whole matrix again: when the values fit in
+     * about half of L2 they are read with normal caching, so terms after
+     * the first find them there; larger matrices stream (evict-first) */
+    const bool cache = (long long)num_diags * stride * 4 <= kL2KeepBytes;
     const float* v = d_x;
     for (int j = 1; j <= m; ++j) {
         float* vn = d_work + (size_t)(j & 1) * (size_t)n;
@@ -214,6 +224,7 @@ extern "C" int dia_expm_taylor(int64_t n, int num_diags, const int* d_offsets, c
         a.y_base = 0;
         a.scale = t / (float)j;
         a.sum = d_y;
+        a.cache_vals = cache;
         const int rc = launch_spmv(a, stream);
         if (rc) return rc;
         v = vn;
