@@ -174,6 +174,9 @@ __device__ __forceinline__ void rp_body(float (&acc)[P + Q - 1][R], const float 
     }
 }
 
+/* D is uniform per run pair: one switch picks the body compiled for it
+ * (both branches are compiled for every R, hence the D % R in the R = 8
+ * cases, which keeps the R = 4 instantiations' template arguments valid) */
 template <int P, int Q, int R>
 __device__ __forceinline__ void rp_dispatch(float (&acc)[P + Q - 1][R], const float (&a)[P][R],
                                             const float* bp, long long B_stride, int lane,
